@@ -1,0 +1,227 @@
+/*
+ * joyomni_b200.h -- C ABI of the B200-native (sm_100a) joyomni_ops hot path.
+ *
+ * Every entry point takes plain device pointers, element counts, element
+ * strides (in elements, not bytes), a dtype code and a cudaStream_t passed as
+ * `void*`, and returns an int status (JO_OK == 0, negative on error).  Nothing
+ * here allocates device memory; outputs are caller-owned.  No C++ exception
+ * crosses this boundary; jo_last_error() returns the message of the last
+ * failing call made on the calling host thread.
+ *
+ * Kernels are compiled for sm_100a only.  A call on any other device fails
+ * with JO_ERR_UNSUPPORTED.
+ *
+ * Each declaration names the reference interface it replaces
+ * (jammm/JoyAI-Video-Edit, paths relative to the reference project root).
+ */
+#ifndef JOYOMNI_B200_H_
+#define JOYOMNI_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define JO_API __attribute__((visibility("default")))
+#else
+#define JO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define JO_OK 0
+#define JO_ERR_INVALID (-1)     /* null pointer, bad option value          */
+#define JO_ERR_SHAPE (-2)       /* sizes inconsistent or out of range      */
+#define JO_ERR_ALIGN (-3)       /* pointer / stride alignment violated     */
+#define JO_ERR_DTYPE (-4)       /* unsupported dtype code                   */
+#define JO_ERR_CUDA (-5)        /* CUDA runtime / launch error              */
+#define JO_ERR_UNSUPPORTED (-6) /* current device is not sm_100             */
+
+/* ---- dtype codes ----------------------------------------------------- */
+#define JO_F32 0
+#define JO_F16 1
+#define JO_BF16 2
+#define JO_E4M3 3 /* float8_e4m3fn */
+
+/* ---- norm codes (fused_norm_scale_shift.cu:153) ---------------------- */
+#define JO_NORM_LAYER 0
+#define JO_NORM_RMS 1
+
+JO_API int jo_abi_version(void);
+JO_API const char* jo_status_name(int status);
+JO_API const char* jo_last_error(void);
+/* Number of kernel launches issued by this library since load (all threads). */
+JO_API uint64_t jo_launch_count(void);
+
+/* ====================================================================== *
+ *  Drop-in replacements of torch.ops.joyomni_ops.* (csrc/pybind.cpp:52-75)
+ * ====================================================================== */
+
+/* rmsnorm: out = x * rsqrt(mean(x^2) + eps) * weight, fp32 math, one rounding.
+ * Replaces joyomni_ops::rmsnorm (joyomni_ops/csrc/rmsnorm.cu:107-126).
+ * x/out: [rows, cols] with row strides; weight: [cols].  dtype: F32/F16/BF16. */
+JO_API int jo_rmsnorm(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,
+               const void* weight, int64_t rows, int64_t cols, int dtype, float eps,
+               void* stream);
+
+/* fused_norm_scale_shift: out = Norm(x; gamma, beta) * (1 + scale) + shift.
+ * Replaces joyomni_ops::fused_norm_scale_shift
+ * (joyomni_ops/csrc/fused_norm_scale_shift.cu:364-403).
+ * norm: JO_NORM_LAYER or JO_NORM_RMS.  gamma/beta: [cols] or NULL (beta is
+ * LayerNorm-only).  scale/shift: [mod_rows, cols] with mod_rows == 1
+ * (broadcast over all rows) or mod_rows == rows, row stride mod_row_stride. */
+JO_API int jo_norm_scale_shift(void* out, int64_t out_row_stride, const void* x, int64_t x_row_stride,
+                        const void* gamma, const void* beta, const void* scale,
+                        const void* shift, int64_t mod_rows, int64_t mod_row_stride,
+                        int64_t rows, int64_t cols, int norm, int dtype, float eps,
+                        void* stream);
+
+/* fused_qk_norm_rope_3d_paired (in place): per head RMSNorm(eps)*weight, then
+ * interleaved-pair RoPE with bf16 cos/sin [seq_len, head_dim/2].  q, k:
+ * contiguous bf16 [batch, seq_len*num_heads, head_dim]; k_pre_rope (optional)
+ * receives the normalised k before rotation.  head_dim in {64, 128, 256}.
+ * Replaces joyomni_ops::fused_qk_norm_rope_3d_paired
+ * (joyomni_ops/csrc/fused_qknorm_rope_3d_kernel.cu:280-319). */
+JO_API int jo_qk_norm_rope_3d_paired(void* q, void* k, int64_t batch, int64_t seq_len,
+                              int64_t num_heads, int64_t head_dim, float eps,
+                              const void* q_weight, const void* k_weight, const void* cos,
+                              const void* sin, void* k_pre_rope, void* stream);
+
+/* A [B=1, L, H, D=128] bf16 view: element (l, h, d) at ptr[l*sl + h*sh + d]. */
+typedef struct jo_view4 {
+  const void* ptr;
+  int64_t len;      /* L */
+  int64_t stride_l; /* elements */
+  int64_t stride_h; /* elements */
+} jo_view4;
+
+/* fused_joint_qkv_pack: out_q = [img_q | RMSNorm(txt_q)], out_k = [cache_k |
+ * img_k | RMSNorm(txt_k)], out_v = [cache_v | img_v | txt_v], all bf16
+ * contiguous [1, *, heads, 128].  The text RMSNorm rounds the normalised value
+ * to bf16 before the weight multiply (double rounding, as the model's RMSNorm).
+ * cache_k.ptr == NULL means no cache.
+ * Replaces joyomni_ops::fused_joint_qkv_pack
+ * (joyomni_ops/csrc/fused_joint_qkv_pack.cu:237-342). */
+JO_API int jo_joint_qkv_pack(void* out_q, void* out_k, void* out_v, jo_view4 img_q, jo_view4 img_k,
+                      jo_view4 img_v, jo_view4 txt_q, jo_view4 txt_k, jo_view4 txt_v,
+                      jo_view4 cache_k, jo_view4 cache_v, const void* txt_q_weight,
+                      const void* txt_k_weight, int64_t heads, float eps, void* stream);
+
+/* fused_cached_kv_pack: concatenates one or two pre-RoPE K/V segments into
+ * contiguous bf16 [1, len0+len1, heads, 128] and applies interleaved RoPE to K
+ * with fp32 full-width cos/sin [len0+len1, 128].  key1.ptr == NULL: one segment.
+ * Replaces joyomni_ops::fused_cached_kv_pack
+ * (joyomni_ops/csrc/fused_joint_qkv_pack.cu:344-415). */
+JO_API int jo_cached_kv_pack(void* out_key, void* out_value, jo_view4 key0, jo_view4 value0,
+                      jo_view4 key1, jo_view4 value1, const float* cos, const float* sin,
+                      int64_t heads, void* stream);
+
+/* sgl_per_token_quant_fp8: per row s = max(amax|x|, 1e-8) / 448 (IEEE fp32),
+ * q = e4m3(clamp(x / s, -448, 448)) (IEEE division, round-to-nearest-even).
+ * These are the semantics of the reference's PyTorch path
+ * (deploy/xvideo/models/dit/fp8_linear.py:38-43); all-zero rows get
+ * s = 1e-8/448 and q = 0.  x: F16/BF16 [rows, cols]; out_q: e4m3 [rows, cols];
+ * out_s: fp32 [rows].
+ * Replaces joyomni_ops::sgl_per_token_quant_fp8
+ * (joyomni_ops/csrc/per_token_quant_fp8.cu:148-176). */
+JO_API int jo_per_token_quant_fp8(void* out_q, int64_t q_row_stride, float* out_s, const void* x,
+                           int64_t x_row_stride, int64_t rows, int64_t cols, int dtype,
+                           void* stream);
+
+/* fp8_scaled_mm: D[m,n] = out_dtype( scale_a[m] * (sum_k A[m,k]*B[k,n]) *
+ * scale_b[n] (+ bias[n]) ), fp32 accumulation in tensor memory (tcgen05).
+ * A: e4m3 row-major [M,K] (row stride lda); B: e4m3 column-major [K,N]
+ * (element (k,n) at b[n*ldb + k]); D row-major [M,N] (row stride ldd).
+ * out_dtype: JO_BF16 or JO_F16; bias (optional) has out_dtype.
+ * K, lda, ldb must be multiples of 16; ldd*esize a multiple of 16 bytes.
+ * Replaces joyomni_ops::fp8_scaled_mm (joyomni_ops/csrc/fp8_gemm.cu:1450-1546,
+ * sm100 path :797-1170). */
+JO_API int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const void* b,
+                     int64_t ldb, const float* scale_a, const float* scale_b,
+                     const void* bias, int64_t m, int64_t n, int64_t k, int out_dtype,
+                     void* stream);
+
+/* ====================================================================== *
+ *  New fused ops on the same path (no single reference kernel)
+ * ====================================================================== */
+
+/* qkv_norm_rope_pack: one pass from the QKV projection output to packed
+ * q/k/v.  qkv: bf16 [tokens, 3*heads*head_dim] (row stride qkv_row_stride),
+ * laid out (K H D) as in dit.py:409-411.  q and k get per-head
+ * RMSNorm(eps)*weight and interleaved RoPE with bf16 cos/sin
+ * [tokens, head_dim/2] (single rounding, as
+ * joyomni_ops/csrc/fused_qknorm_rope_3d_kernel.cu:200-231); v is copied.
+ * Output element (h, t, d) of q/k/v is written at out[h*out_stride_h +
+ * t*out_stride_t + d]: head-major [heads, tokens, D] is (tokens*D, D),
+ * token-major [tokens, heads, D] is (D, heads*D).  k_pre_rope (optional,
+ * same layout) receives normalised k before rotation.  head_dim in {64,128,256}.
+ * Replaces the chain deploy/xvideo/models/dit/dit.py:408-429 ->
+ * sgl_fused_ops.py:137-168 (two .contiguous() copies + the paired kernel) and
+ * the q/k/v part of fused_joint_qkv_pack. */
+JO_API int jo_qkv_norm_rope_pack(void* out_q, void* out_k, void* out_v, void* k_pre_rope,
+                          int64_t out_stride_h, int64_t out_stride_t, const void* qkv,
+                          int64_t qkv_row_stride, int64_t tokens, int64_t heads,
+                          int64_t head_dim, const void* q_weight, const void* k_weight,
+                          const void* cos, const void* sin, float eps, void* stream);
+
+/* gated residual: out = residual + x * gate (fp32 math, one rounding); gate is
+ * [gate_rows, cols] with gate_rows in {1, rows}.
+ * Replaces fused_add_gate = torch.addcmul
+ * (deploy/xvideo/models/dit/sgl_fused_ops.py:302-305). */
+JO_API int jo_gated_residual(void* out, int64_t out_row_stride, const void* residual,
+                      int64_t res_row_stride, const void* x, int64_t x_row_stride,
+                      const void* gate, int64_t gate_rows, int64_t gate_row_stride,
+                      int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* gated residual + Norm + modulate, one pass:
+ *   h   = dtype(residual + x * gate)           (written to out_h)
+ *   out = Norm(h; gamma, beta) * (1 + scale) + shift
+ * Replaces dit.py:525-534 (fused_add_gate followed by fused_layernorm_modulate). */
+JO_API int jo_gated_residual_norm_scale_shift(
+    void* out_h, int64_t h_row_stride, void* out, int64_t out_row_stride,
+    const void* residual, int64_t res_row_stride, const void* x, int64_t x_row_stride,
+    const void* gate, int64_t gate_rows, int64_t gate_row_stride, const void* gamma,
+    const void* beta, const void* scale, const void* shift, int64_t mod_rows,
+    int64_t mod_row_stride, int64_t rows, int64_t cols, int norm, int dtype, float eps,
+    void* stream);
+
+/* GELU, tanh approximation: out = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+ * Replaces F.gelu(x, approximate="tanh") (deploy/xvideo/models/dit/dit.py:87-89). */
+JO_API int jo_gelu_tanh(void* out, const void* x, int64_t n, int dtype, void* stream);
+
+/* SiLU-gated multiply: out[r, c] = silu(a[r, c]) * b[r, c] (fp32 math). */
+JO_API int jo_silu_mul(void* out, int64_t out_row_stride, const void* a, int64_t a_row_stride,
+                const void* b, int64_t b_row_stride, int64_t rows, int64_t cols, int dtype,
+                void* stream);
+
+/* Sinusoidal timestep embedding (the diffusers Timesteps projection used at
+ * deploy/xvideo/models/dit/dit.py:574-575,614): out fp32 [batch, dim],
+ * freq_i = exp(-ln(max_period) * i / (dim/2 - downscale_freq_shift)),
+ * e = [sin(scale*t*f), cos(scale*t*f)], halves swapped when flip_sin_to_cos. */
+JO_API int jo_timestep_embedding(float* out, const float* t, int64_t batch, int64_t dim,
+                          int flip_sin_to_cos, float downscale_freq_shift, float scale,
+                          float max_period, void* stream);
+
+/* RMSNorm -> per-token FP8 quant, one pass: y = dtype(rmsnorm(x)*w) is rounded
+ * to dtype in registers, then quantised with the jo_per_token_quant_fp8
+ * semantics.  Oracle: quant(_torch_rmsnorm(x, w, eps)). */
+JO_API int jo_rmsnorm_quant_fp8(void* out_q, int64_t q_row_stride, float* out_s, const void* x,
+                         int64_t x_row_stride, const void* weight, int64_t rows, int64_t cols,
+                         int dtype, float eps, void* stream);
+
+/* Norm + modulate -> per-token FP8 quant, one pass (the input of every
+ * Fp8Linear QKV / MLP-up projection, dit.py:402-408 and :529-535 ->
+ * fp8_linear.py:133-140): y = dtype(Norm(x)*(1+scale)+shift), then quantised. */
+JO_API int jo_norm_scale_shift_quant_fp8(void* out_q, int64_t q_row_stride, float* out_s,
+                                  const void* x, int64_t x_row_stride, const void* gamma,
+                                  const void* beta, const void* scale, const void* shift,
+                                  int64_t mod_rows, int64_t mod_row_stride, int64_t rows,
+                                  int64_t cols, int norm, int dtype, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JOYOMNI_B200_H_ */

@@ -1,0 +1,92 @@
+// Host-side plumbing shared by every entry point: error strings, per-device
+// facts, launch accounting.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+thread_local char g_last_error[512] = "";
+std::atomic<uint64_t> g_launches{0};
+
+constexpr int kMaxDevices = 64;
+jo::DeviceInfo g_info[kMaxDevices];
+std::once_flag g_info_once[kMaxDevices];
+int g_info_status[kMaxDevices];
+}  // namespace
+
+namespace jo {
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int after_launch(const char* what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(JO_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return JO_OK;
+}
+
+int device_info(const DeviceInfo** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(JO_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(JO_ERR_CUDA, "device index %d out of range", dev);
+  std::call_once(g_info_once[dev], [dev]() {
+    DeviceInfo& d = g_info[dev];
+    cudaError_t r = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (r == cudaSuccess)
+      r = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    g_info_status[dev] = (r == cudaSuccess) ? JO_OK : JO_ERR_CUDA;
+  });
+  if (g_info_status[dev] != JO_OK) return fail(JO_ERR_CUDA, "device %d: attribute query failed", dev);
+  const DeviceInfo& d = g_info[dev];
+  if (d.major != 10 || d.minor != 0)
+    return fail(JO_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
+                d.major, d.minor);
+  *out = &d;
+  return JO_OK;
+}
+
+int occupancy(const void* kernel, int threads, size_t smem) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  return n > 0 ? n : 1;
+}
+
+}  // namespace jo
+
+extern "C" {
+
+int jo_abi_version(void) { return 1; }
+
+const char* jo_status_name(int status) {
+  switch (status) {
+    case JO_OK: return "JO_OK";
+    case JO_ERR_INVALID: return "JO_ERR_INVALID";
+    case JO_ERR_SHAPE: return "JO_ERR_SHAPE";
+    case JO_ERR_ALIGN: return "JO_ERR_ALIGN";
+    case JO_ERR_DTYPE: return "JO_ERR_DTYPE";
+    case JO_ERR_CUDA: return "JO_ERR_CUDA";
+    case JO_ERR_UNSUPPORTED: return "JO_ERR_UNSUPPORTED";
+    default: return "JO_ERR_UNKNOWN";
+  }
+}
+
+const char* jo_last_error(void) { return g_last_error; }
+
+uint64_t jo_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"

@@ -1,0 +1,179 @@
+// Shared device/host helpers for the sm_100a joyomni kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "joyomni_b200.h"
+
+namespace jo {
+
+// ---------------------------------------------------------------- host side
+// Records `fmt` as the thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Checks cudaGetLastError() after a launch; counts the launch.
+int after_launch(const char* what);
+// Per-device facts, cached on first use.  Returns JO_OK or an error status.
+struct DeviceInfo {
+  int sm_count;
+  int major, minor;
+  int max_smem_optin;
+};
+int device_info(const DeviceInfo** out);
+// Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes.
+int occupancy(const void* kernel, int threads, size_t smem);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case JO_F32: return 4;
+    case JO_F16: return 2;
+    case JO_BF16: return 2;
+    case JO_E4M3: return 1;
+    default: return 0;
+  }
+}
+
+// ---------------------------------------------------------------- device side
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Sum over aligned groups of G lanes (G a power of two <= 32).
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// 16-byte global accesses.  Read-once data uses the non-coherent path without
+// L1 allocation; broadcast operands use plain __ldg.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 ld_bcast(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_global(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// Element traits: 16-byte vectors of T, conversion to/from fp32.
+template <typename T>
+struct Elt;
+template <>
+struct Elt<float> {
+  static constexpr int kVec = 4;
+  __device__ __forceinline__ static float to_f(float v) { return v; }
+  __device__ __forceinline__ static float from_f(float v) { return v; }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+};
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+struct Elt<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+  }
+};
+template <>
+struct Elt<__half> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float to_f(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_f(float v) { return __float2half_rn(v); }
+  __device__ __forceinline__ static void unpack(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 t = __half22float2(h);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  __device__ __forceinline__ static uint4 pack(const float* f) {
+    return make_uint4(pack_f16x2(f[0], f[1]), pack_f16x2(f[2], f[3]), pack_f16x2(f[4], f[5]),
+                      pack_f16x2(f[6], f[7]));
+  }
+};
+
+// Round a float through T and back (the value a bf16/fp16 tensor would hold).
+template <typename T>
+__device__ __forceinline__ float round_through(float v) {
+  return Elt<T>::to_f(Elt<T>::from_f(v));
+}
+template <>
+__device__ __forceinline__ float round_through<float>(float v) {
+  return v;
+}
+
+// e4m3 (float8_e4m3fn) conversion of two floats, round-to-nearest-even with
+// saturation to +-448; `lo` lands in the low byte.
+__device__ __forceinline__ uint16_t e4m3x2(float lo, float hi) {
+  __nv_fp8x2_storage_t s = __nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+  return static_cast<uint16_t>(s);
+}
+
+// Per-token quantisation helpers, semantics of fp8_linear.py:38-43:
+//   scale = max(amax, 1e-8) / 448 ; q = e4m3(clamp(x / scale, -448, 448)).
+constexpr float kFp8Max = 448.0f;
+__device__ __forceinline__ float quant_scale(float amax) {
+  return __fdiv_rn(fmaxf(amax, 1e-8f), kFp8Max);
+}
+__device__ __forceinline__ float quant_clamp(float x, float scale) {
+  float v = __fdiv_rn(x, scale);
+  return fminf(fmaxf(v, -kFp8Max), kFp8Max);
+}
+
+// 1/sqrt(v) rounded as torch's CPU rsqrt (IEEE sqrt, then IEEE reciprocal).
+__device__ __forceinline__ float rsqrt_ieee(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
+
+}  // namespace jo
+
+#define JO_CHECK_ARG(cond, code, ...)              \
+  do {                                             \
+    if (!(cond)) return ::jo::fail(code, __VA_ARGS__); \
+  } while (0)

@@ -1,0 +1,248 @@
+"""joyomni_ops -- B200-native (sm_100a) drop-in for JoyAI-Video-Edit's op library.
+
+Same import name, same ``torch.ops.joyomni_ops`` schemas, same Python wrappers
+and FakeTensor registrations as the reference package
+(joyomni_ops/joyomni_ops/__init__.py:1-153, schemas joyomni_ops/csrc/pybind.cpp:52-75),
+so ``deploy/xvideo/models/dit/sgl_fused_ops.py`` and ``fp8_linear.py`` bind to it
+unchanged.  Every op is a hand-written sm_100a CUDA kernel in
+``libjoyomni_b200.so`` reached through its C ABI (``include/joyomni_b200.h``);
+``_C.so`` only registers the torch ops.  There is no CPU or eager fallback: the
+ops are registered for the CUDA dispatch key only, and importing without the
+built extension raises ImportError exactly like the reference.
+
+New fused ops on the same path live in the same namespace
+(``qkv_norm_rope_pack``, ``gated_residual``, ``gated_residual_norm_scale_shift``,
+``gelu_tanh``, ``silu_mul``, ``timestep_embedding``, ``rmsnorm_quant_fp8``,
+``norm_scale_shift_quant_fp8``).
+"""
+import glob
+import os
+from typing import Optional
+
+import torch
+
+_here = os.path.dirname(__file__)
+_so = glob.glob(os.path.join(_here, "_C*.so"))
+if not _so:
+    raise ImportError(f"joyomni_ops C extension not found in {_here}; build it first (python build.py)")
+torch.ops.load_library(_so[0])
+
+__all__ = [
+    "fused_qk_norm_rope_3d_paired",
+    "fused_joint_qkv_pack",
+    "fused_cached_kv_pack",
+    "fused_norm_scale_shift",
+    "rmsnorm",
+    "sgl_per_token_quant_fp8",
+    "fp8_scaled_mm",
+    "has_quant",
+    "has_fp8",
+    # new fused ops
+    "qkv_norm_rope_pack",
+    "gated_residual",
+    "gated_residual_norm_scale_shift",
+    "gelu_tanh",
+    "silu_mul",
+    "timestep_embedding",
+    "rmsnorm_quant_fp8",
+    "norm_scale_shift_quant_fp8",
+    "library_path",
+]
+
+_ops = torch.ops.joyomni_ops
+
+
+def library_path() -> str:
+    """Path of the C-ABI library (libjoyomni_b200.so) these ops call."""
+    return os.path.join(_here, "libjoyomni_b200.so")
+
+
+# ---------------------------------------------------------------- fake kernels
+# As in the reference (joyomni_ops/__init__.py:36-101): FakeTensor kernels keep
+# the native ops opaque inside one torch.compile graph.
+@torch.library.register_fake("joyomni_ops::fused_qk_norm_rope_3d_paired")
+def _fake_fused_qk_norm_rope_3d_paired(q, k, seq_len, num_heads, eps, q_weight, k_weight, cos, sin,
+                                       k_pre_rope=None):
+    return None
+
+
+@torch.library.register_fake("joyomni_ops::fused_joint_qkv_pack")
+def _fake_fused_joint_qkv_pack(img_q, img_k, img_v, txt_q, txt_k, txt_v, cached_k, cached_v,
+                               txt_q_weight, txt_k_weight, eps):
+    batch, img_len, heads, head_dim = img_q.shape
+    txt_len = txt_q.shape[1]
+    cache_len = cached_k.shape[1] if cached_k is not None else 0
+    out_q = img_q.new_empty((batch, img_len + txt_len, heads, head_dim))
+    out_k = img_q.new_empty((batch, cache_len + img_len + txt_len, heads, head_dim))
+    return out_q, out_k, torch.empty_like(out_k)
+
+
+@torch.library.register_fake("joyomni_ops::fused_cached_kv_pack")
+def _fake_fused_cached_kv_pack(key0, value0, key1, value1, cos, sin):
+    batch, len0, heads, head_dim = key0.shape
+    len1 = key1.shape[1] if key1 is not None else 0
+    out_key = key0.new_empty((batch, len0 + len1, heads, head_dim))
+    return out_key, torch.empty_like(out_key)
+
+
+@torch.library.register_fake("joyomni_ops::fused_norm_scale_shift")
+def _fake_fused_norm_scale_shift(x, gamma, beta, scale, shift, norm_type, eps):
+    return x.new_empty(x.shape)
+
+
+@torch.library.register_fake("joyomni_ops::rmsnorm")
+def _fake_rmsnorm(x, weight, eps):
+    return x.new_empty(x.shape)
+
+
+@torch.library.register_fake("joyomni_ops::sgl_per_token_quant_fp8")
+def _fake_sgl_per_token_quant_fp8(input, output_q, output_s):
+    return None
+
+
+@torch.library.register_fake("joyomni_ops::fp8_scaled_mm")
+def _fake_fp8_scaled_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias=None):
+    return mat_a.new_empty((mat_a.shape[0], mat_b.shape[1]), dtype=out_dtype)
+
+
+@torch.library.register_fake("joyomni_ops::qkv_norm_rope_pack")
+def _fake_qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, head_major, k_pre_rope=None):
+    L = qkv.shape[0]
+    D = qkv.shape[1] // (3 * num_heads)
+    shape = (num_heads, L, D) if head_major else (L, num_heads, D)
+    return qkv.new_empty(shape), qkv.new_empty(shape), qkv.new_empty(shape)
+
+
+@torch.library.register_fake("joyomni_ops::gated_residual")
+def _fake_gated_residual(residual, x, gate):
+    return residual.new_empty(residual.shape)
+
+
+@torch.library.register_fake("joyomni_ops::gated_residual_norm_scale_shift")
+def _fake_gated_residual_norm_scale_shift(residual, x, gate, gamma, beta, scale, shift, norm_type, eps):
+    return residual.new_empty(residual.shape), residual.new_empty(residual.shape)
+
+
+@torch.library.register_fake("joyomni_ops::gelu_tanh")
+def _fake_gelu_tanh(x):
+    return x.new_empty(x.shape)
+
+
+@torch.library.register_fake("joyomni_ops::silu_mul")
+def _fake_silu_mul(a, b):
+    return a.new_empty(a.shape)
+
+
+@torch.library.register_fake("joyomni_ops::timestep_embedding")
+def _fake_timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period):
+    return t.new_empty((t.shape[0], dim), dtype=torch.float32)
+
+
+@torch.library.register_fake("joyomni_ops::rmsnorm_quant_fp8")
+def _fake_rmsnorm_quant_fp8(x, weight, eps):
+    return (x.new_empty(x.shape, dtype=torch.float8_e4m3fn),
+            x.new_empty((x.shape[0], 1), dtype=torch.float32))
+
+
+@torch.library.register_fake("joyomni_ops::norm_scale_shift_quant_fp8")
+def _fake_norm_scale_shift_quant_fp8(x, gamma, beta, scale, shift, norm_type, eps):
+    return (x.new_empty(x.shape, dtype=torch.float8_e4m3fn),
+            x.new_empty((x.shape[0], 1), dtype=torch.float32))
+
+
+# ---------------------------------------------------------------- wrappers (reference signatures)
+def fused_qk_norm_rope_3d_paired(q, k, seq_len, num_heads, eps, q_weight, k_weight, cos, sin, k_pre_rope=None):
+    """In-place fused RMSNorm(q,k) + 3D RoPE. q/k: [B, seq_len*num_heads, head_dim] bf16."""
+    _ops.fused_qk_norm_rope_3d_paired(q, k, seq_len, num_heads, eps, q_weight, k_weight, cos, sin, k_pre_rope)
+
+
+def fused_joint_qkv_pack(img_q, img_k, img_v, txt_q, txt_k, txt_v, cached_k, cached_v, txt_q_weight,
+                         txt_k_weight, eps=1e-6):
+    """Pack joint-attention Q/K/V and fuse text Q/K RMSNorm (bf16, B=1, D=128)."""
+    return _ops.fused_joint_qkv_pack(img_q, img_k, img_v, txt_q, txt_k, txt_v, cached_k, cached_v,
+                                     txt_q_weight, txt_k_weight, eps)
+
+
+def fused_cached_kv_pack(key0, value0, key1, value1, cos, sin):
+    """Rotate and pack one or two pre-RoPE cache segments (bf16, B=1, D=128)."""
+    return _ops.fused_cached_kv_pack(key0, value0, key1, value1, cos, sin)
+
+
+def _norm_code(norm_type: str) -> int:
+    # joyomni_ops/__init__.py:129-132: unknown strings become -1, which the op rejects.
+    return 0 if norm_type == "layer" else 1 if norm_type == "rms" else -1
+
+
+def fused_norm_scale_shift(x, gamma, beta, scale, shift, norm_type, eps=1e-5):
+    """Norm(x; gamma, beta) * (1 + scale) + shift. norm_type: 'layer' or 'rms'."""
+    return _ops.fused_norm_scale_shift(x, gamma, beta, scale, shift, _norm_code(norm_type), eps)
+
+
+def rmsnorm(x, weight, eps=1e-6):
+    """(x / RMS(x)) * weight. x: [M, N], weight: [N]."""
+    return _ops.rmsnorm(x, weight, eps)
+
+
+def has_fp8() -> bool:
+    return hasattr(_ops, "fp8_scaled_mm")
+
+
+def has_quant() -> bool:
+    return hasattr(_ops, "sgl_per_token_quant_fp8")
+
+
+def sgl_per_token_quant_fp8(input, output_q, output_s):
+    _ops.sgl_per_token_quant_fp8(input, output_q, output_s)
+
+
+def fp8_scaled_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None):
+    return _ops.fp8_scaled_mm(mat_a, mat_b, scales_a, scales_b, out_dtype, bias)
+
+
+# ---------------------------------------------------------------- new fused ops
+def qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps=1e-6, head_major=True,
+                       k_pre_rope: Optional[torch.Tensor] = None):
+    """qkv [L, 3*H*D] (K H D order) -> q, k, v with per-head RMSNorm + RoPE on q/k.
+
+    Outputs are [H, L, D] (head_major=True) or [L, H, D].  cos/sin: bf16 [L, D/2].
+    k_pre_rope, if given, receives the normalised k before rotation (same layout).
+    """
+    return _ops.qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, head_major, k_pre_rope)
+
+
+def gated_residual(residual, x, gate):
+    """residual + x * gate (torch.addcmul(residual, x, gate)), gate broadcast over rows."""
+    return _ops.gated_residual(residual, x, gate)
+
+
+def gated_residual_norm_scale_shift(residual, x, gate, scale, shift, norm_type="layer", eps=1e-6,
+                                    gamma=None, beta=None):
+    """(h, Norm(h)*(1+scale)+shift) with h = residual + x*gate, in one pass."""
+    return _ops.gated_residual_norm_scale_shift(residual, x, gate, gamma, beta, scale, shift,
+                                                _norm_code(norm_type), eps)
+
+
+def gelu_tanh(x):
+    """F.gelu(x, approximate='tanh')."""
+    return _ops.gelu_tanh(x)
+
+
+def silu_mul(a, b):
+    """silu(a) * b."""
+    return _ops.silu_mul(a, b)
+
+
+def timestep_embedding(t, dim=256, flip_sin_to_cos=True, downscale_freq_shift=0.0, scale=1.0,
+                       max_period=10000.0):
+    """Sinusoidal timestep projection (diffusers Timesteps), fp32 [B, dim]."""
+    return _ops.timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period)
+
+
+def rmsnorm_quant_fp8(x, weight, eps=1e-6):
+    """(q e4m3 [M, N], scale fp32 [M, 1]) of bf16(rmsnorm(x) * weight)."""
+    return _ops.rmsnorm_quant_fp8(x, weight, eps)
+
+
+def norm_scale_shift_quant_fp8(x, gamma, beta, scale, shift, norm_type="layer", eps=1e-6):
+    """(q e4m3 [M, N], scale fp32 [M, 1]) of bf16(Norm(x)*(1+scale)+shift)."""
+    return _ops.norm_scale_shift_quant_fp8(x, gamma, beta, scale, shift, _norm_code(norm_type), eps)
