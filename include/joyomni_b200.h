@@ -54,6 +54,11 @@ JO_API const char* jo_status_name(int status);
 JO_API const char* jo_last_error(void);
 /* Number of kernel launches issued by this library since load (all threads). */
 JO_API uint64_t jo_launch_count(void);
+/* Device-side faults recorded on the current device since the last call (then
+ * cleared): a kernel whose bounded wait on an mbarrier expired counts one,
+ * stops issuing work, frees its tensor memory and returns instead of hanging.
+ * Synchronises the current device. */
+JO_API int jo_device_fault_count(uint32_t* count);
 
 /* ====================================================================== *
  *  Drop-in replacements of torch.ops.joyomni_ops.* (csrc/pybind.cpp:52-75)

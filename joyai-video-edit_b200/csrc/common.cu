@@ -7,6 +7,11 @@
 
 #include "common.cuh"
 
+// Bounded-wait expiries of this library's kernels on each device (one copy
+// per device context); kernels receive its address, jo_device_fault_count
+// reads and clears it.
+__device__ unsigned int g_jo_faults = 0;
+
 namespace {
 thread_local char g_last_error[512] = "";
 std::atomic<uint64_t> g_launches{0};
@@ -46,6 +51,7 @@ int device_info(const DeviceInfo** out) {
     if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
     if (r == cudaSuccess)
       r = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (r == cudaSuccess && d.major == 10) r = cudaGetSymbolAddress((void**)&d.fault, g_jo_faults);
     g_info_status[dev] = (r == cudaSuccess) ? JO_OK : JO_ERR_CUDA;
   });
   if (g_info_status[dev] != JO_OK) return fail(JO_ERR_CUDA, "device %d: attribute query failed", dev);
@@ -88,5 +94,17 @@ const char* jo_status_name(int status) {
 const char* jo_last_error(void) { return g_last_error; }
 
 uint64_t jo_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int jo_device_fault_count(uint32_t* count) {
+  if (!count) return jo::fail(JO_ERR_INVALID, "device_fault_count: null pointer");
+  const jo::DeviceInfo* di;
+  if (int s = jo::device_info(&di)) return s;
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpy(&v, di->fault, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(di->fault, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return jo::fail(JO_ERR_CUDA, "device_fault_count: %s", cudaGetErrorString(e));
+  *count = v;
+  return JO_OK;
+}
 
 }  // extern "C"

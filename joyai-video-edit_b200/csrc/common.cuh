@@ -21,6 +21,7 @@ struct DeviceInfo {
   int sm_count;
   int major, minor;
   int max_smem_optin;
+  unsigned int* fault;  // device address of this device's fault counter
 };
 int device_info(const DeviceInfo** out);
 // Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes.

@@ -1,6 +1,402 @@
-// Placeholder until the tcgen05 GEMM lands.
-#include "common.cuh"
-extern "C" int jo_fp8_scaled_mm(void*, int64_t, const void*, int64_t, const void*, int64_t, const float*,
-                                const float*, const void*, int64_t, int64_t, int64_t, int, void*) {
-  return jo::fail(JO_ERR_UNSUPPORTED, "fp8_scaled_mm: not built yet");
+// FP8 (e4m3) row/column-scaled GEMM on the 5th-generation tensor cores.
+//
+//   D[m, n] = out( scale_a[m] * (sum_k A[m, k] * B[k, n]) * scale_b[n] (+ bias[n]) )
+//
+// Replaces joyomni_ops::fp8_scaled_mm (joyomni_ops/csrc/fp8_gemm.cu:1450-1546),
+// whose sm100 path is a CUTLASS collective with 2x2x1 clusters and TMA
+// multicast (:1015-1159).  This kernel is written directly against the
+// sm_100a instructions and uses NO cluster multicast:
+//
+//   * persistent: one CTA per SM walks output tiles of 128 x 256;
+//   * warp 0, one lane: TMA producer.  A tile 128 x 128 B and B tile 256 x 128 B
+//     per k-block (128-byte swizzle, K-major), kStages-deep mbarrier ring;
+//   * warp 1, one lane: issues tcgen05.mma.cta_group::1.kind::f8f6f4
+//     (128 x 256 x 32 per instruction, fp32 accumulator in tensor memory) and
+//     tcgen05.commit to release smem stages / publish finished accumulators;
+//     warp 1 also owns the 512-column TMEM allocation (two 256-column
+//     accumulators, so the epilogue of tile i overlaps the mainloop of tile i+1);
+//   * warps 2-5: epilogue.  tcgen05.ld 32 lanes x 32 columns at a time, apply
+//     the EVT order of the reference ((acc * sB) * sA (+ bias), fp32), round to
+//     bf16/fp16 and store 64 contiguous bytes per thread.
+//
+// Every mbarrier wait is bounded (kWaitNs of wall time, pipeline.cuh); on
+// expiry the kernel records the fault in the per-device counter (read by
+// jo_device_fault_count), stops issuing work, drains its own TMA copies, frees
+// its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "pipeline.cuh"
+
+namespace jo {
+namespace {
+
+constexpr int kBM = 128;       // UMMA M (one CTA)
+constexpr int kBN = 256;       // UMMA N
+constexpr int kBK = 128;       // bytes of K per stage = one 128-byte swizzle row
+constexpr int kUmmaK = 32;     // K per tcgen05.mma kind::f8f6f4
+constexpr int kStages = 4;
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kTmemCols = 512;  // 2 accumulators x 256 fp32 columns
+constexpr int kStageA = kBM * kBK;  // 16 KB
+constexpr int kStageB = kBN * kBK;  // 32 KB
+constexpr int kSmemBytes = kStages * (kStageA + kStageB) + 1024 /*align*/ + 256 /*barriers*/;
+
+// ------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+// D(tmem) (+)= A(smem) * B(smem)^T, both K-major
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row
+// groups 1024 B apart (SBO), LBO unused (1), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;              // leading byte offset (ignored for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
+  d |= (uint64_t)1 << 46;              // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;              // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: e4m3 x e4m3 -> f32, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
+                            | (0u << 7) | (0u << 10)          // A, B: e4m3
+                            | ((uint32_t)(kBN >> 3) << 17)    // N >> 3
+                            | ((uint32_t)(kBM >> 4) << 24);   // M >> 4
+
+struct GemmArgs {
+  void* d;
+  int64_t ldd;
+  const float* sa;
+  const float* sb;
+  const void* bias;
+  int m, n, k;
+  int tiles_m, tiles_n;
+  unsigned int* fault;
+};
+
+template <typename OutT>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  return pack_bf16x2(a, b);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  return pack_f16x2(a, b);
+}
+
+template <typename OutT, bool kBias>
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const GemmArgs args) {
+  unsigned int* const fault = args.fault;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw_base);
+  const uint32_t sA = base;                        // kStages x 16 KB
+  const uint32_t sB = base + kStages * kStageA;    // kStages x 32 KB
+  const uint32_t bars = sB + kStages * kStageB;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (kStages + s); };
+  auto tfull_bar = [&](int b) { return bars + 8u * (2 * kStages + b); };
+  auto tempty_bar = [&](int b) { return bars + 8u * (2 * kStages + 2 + b); };
+  const uint32_t done_bar = bars + 8u * (2 * kStages + 4);  // all MMAs of this CTA retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * kStages + 5));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int kblocks = (args.k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 4 * 32);
+    }
+    mbar_init(done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_phase[kStages];
+      bool issued[kStages];
+      for (int s = 0; s < kStages; ++s) issued[s] = false;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, fault)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(full_bar(stage), kStageA + kStageB);
+          tma_load_2d(sA + stage * kStageA, &map_a, kb * kBK, tm * kBM, full_bar(stage));
+          tma_load_2d(sB + stage * kStageB, &map_b, kb * kBK, tn * kBN, full_bar(stage));
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // drain: every copy this thread issued must have landed before the CTA exits
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s]) mbar_wait(full_bar(s), issued_phase[s], fault);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, fault)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, fault)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * kStageA, b0 = sB + stage * kStageB;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            tc_mma(d_tmem, sw128_desc(a0 + kk * kUmmaK), sw128_desc(b0 + kk * kUmmaK), kIdesc,
+                   (kb | kk) != 0);
+          tc_commit(empty_bar(stage));  // stage reusable once these MMAs have read it
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(tfull_bar(acc));  // accumulator complete
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // TMEM is freed below: wait until every MMA this thread issued has retired
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, fault);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, TMEM lanes 32*(warp%4) .. +31
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    OutT* D = reinterpret_cast<OutT*>(args.d);
+    const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
+      tc_fence_after();
+      const int row = tm * kBM + q * 32 + lane;
+      const bool row_ok = row < args.m;
+      const float s_a = row_ok ? __ldg(args.sa + row) : 0.f;
+      OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        const int n0 = tn * kBN + c * 32;
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        if (n0 >= args.n) continue;  // whole chunk past N (uniform across the warp)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+          const int ng = n0 + g * 8;
+          if (ng >= args.n) break;
+          const float4 sb0 = __ldg(reinterpret_cast<const float4*>(args.sb + ng));
+          const float4 sb1 = __ldg(reinterpret_cast<const float4*>(args.sb + ng + 4));
+          const float sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
+          float bv[8];
+          if constexpr (kBias) {
+            float t[8];
+            Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(bias + ng)), t);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) bv[e] = t[e];
+          }
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float t = __uint_as_float(r[g * 8 + e]) * sb[e];
+            o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
+          }
+          if (row_ok) {
+            uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
+                                 pack2<OutT>(o[6], o[7]));
+            *reinterpret_cast<uint4*>(drow + ng) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major fp8 operand [rows, K] (row stride ld bytes), box kBK x box_rows, 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_t ld, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(JO_ERR_CUDA, "fp8_scaled_mm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(JO_ERR_CUDA, "fp8_scaled_mm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return JO_OK;
+}
+
+template <typename OutT, bool kBias>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st,
+                const DeviceInfo* di) {
+  auto kern = fp8_gemm_kernel<OutT, kBias>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+      return fail(JO_ERR_CUDA, "fp8_scaled_mm: cannot reserve %d bytes of shared memory", kSmemBytes);
+    attr = true;
+  }
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int grid = tiles < di->sm_count ? tiles : di->sm_count;
+  kern<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, a);
+  return after_launch("fp8_gemm_kernel");
+}
+
+}  // namespace
+}  // namespace jo
+
+using namespace jo;
+
+extern "C" {
+
+int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
+                     const float* scale_a, const float* scale_b, const void* bias, int64_t m, int64_t n,
+                     int64_t k, int out_dtype, void* stream) {
+  const char* op = "fp8_scaled_mm";
+  const DeviceInfo* di;
+  if (int s = device_info(&di)) return s;
+  if (m < 0 || n < 0 || k < 0) return fail(JO_ERR_SHAPE, "%s: negative size", op);
+  if (m == 0 || n == 0) return JO_OK;
+  if (out_dtype != JO_BF16 && out_dtype != JO_F16) return fail(JO_ERR_DTYPE, "%s: out dtype must be bf16/fp16", op);
+  if (!d || !a || !b || !scale_a || !scale_b) return fail(JO_ERR_INVALID, "%s: null operand", op);
+  if (k == 0) return fail(JO_ERR_SHAPE, "%s: K must be positive", op);
+  if (k % 16 || lda % 16 || ldb % 16) return fail(JO_ERR_ALIGN, "%s: K, lda, ldb must be multiples of 16", op);
+  if (n % 8 || ldd % 8) return fail(JO_ERR_ALIGN, "%s: N and ldd must be multiples of 8", op);
+  if (lda < k || ldb < k || ldd < n) return fail(JO_ERR_SHAPE, "%s: leading dimension smaller than the row", op);
+  if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: size too large", op);
+  if (!aligned16(d) || !aligned16(a) || !aligned16(b) || !aligned16(scale_b) || (bias && !aligned16(bias)))
+    return fail(JO_ERR_ALIGN, "%s: D, A, B, scale_b and bias must be 16-byte aligned", op);
+  CUtensorMap ma, mb;
+  if (int s = make_map(&ma, a, m, k, lda, kBM)) return s;
+  if (int s = make_map(&mb, b, n, k, ldb, kBN)) return s;
+  GemmArgs g{};
+  g.d = d;
+  g.ldd = ldd;
+  g.sa = scale_a;
+  g.sb = scale_b;
+  g.bias = bias;
+  g.m = (int)m;
+  g.n = (int)n;
+  g.k = (int)k;
+  g.tiles_m = (int)cdiv(m, kBM);
+  g.tiles_n = (int)cdiv(n, kBN);
+  g.fault = di->fault;
+  if ((int64_t)g.tiles_m * g.tiles_n > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many tiles", op);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (out_dtype == JO_BF16)
+    return bias ? launch_gemm<__nv_bfloat16, true>(ma, mb, g, st, di) : launch_gemm<__nv_bfloat16, false>(ma, mb, g, st, di);
+  return bias ? launch_gemm<__half, true>(ma, mb, g, st, di) : launch_gemm<__half, false>(ma, mb, g, st, di);
+}
+
+}  // extern "C"

@@ -1,0 +1,88 @@
+// mbarrier / bulk-copy (TMA) primitives shared by the staged kernels.
+//
+// Every wait is bounded: after kWaitNs of wall time without the phase
+// completing, the waiter increments the per-device fault counter (whose device
+// address every kernel receives as an argument, read back by
+// jo_device_fault_count) and returns false, so a protocol error ends the
+// kernel with a recorded fault instead of a hung GPU.
+#pragma once
+
+#include "common.cuh"
+
+namespace jo {
+
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+// Make barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* fault) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0 && globaltimer() - t0 > kWaitNs) {
+      atomicAdd(fault, 1u);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16),
+// completion signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+// Ring of kSlots shared-memory slots fed by one producer thread with bulk
+// copies and drained by consumer warps.  Unit i of this CTA lives in slot
+// i % kSlots during its phase (i / kSlots) & 1.
+struct Ring {
+  uint32_t data;  // slot 0 data (shared address)
+  uint32_t bars;  // full[kSlots] then empty[kSlots]
+  uint32_t slot_bytes;
+  int slots;
+  __device__ __forceinline__ uint32_t slot(int i) const { return data + (uint32_t)(i % slots) * slot_bytes; }
+  __device__ __forceinline__ uint32_t full(int i) const { return bars + 8u * (uint32_t)(i % slots); }
+  __device__ __forceinline__ uint32_t empty(int i) const { return bars + 8u * (uint32_t)(slots + i % slots); }
+  __device__ __forceinline__ uint32_t parity(int i) const { return (uint32_t)((i / slots) & 1); }
+};
+
+}  // namespace jo

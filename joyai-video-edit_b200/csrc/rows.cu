@@ -8,15 +8,16 @@
 //   per-token FP8 quant              deploy/xvideo/models/dit/fp8_linear.py:38-43
 //   rmsnorm / norm+modulate -> FP8   (fusions of the above)
 //
-// Design (B200): the op is HBM-bound, so each row is read from HBM exactly
-// once with 16-byte non-coherent loads, kept in registers across the
-// reduction(s), and written once with 16-byte stores.  Rows of up to 512
-// vectors (4096 bf16) are owned by a single warp (no shared memory, no block
-// barrier; 8 rows per 256-thread CTA); longer rows are owned by a CTA.  All
-// loads of a row are issued before the first use so every thread keeps up to
-// 16 x 16 B in flight.  Shapes that break 16-byte alignment take a scalar
-// block-per-row path that re-reads the row from global memory.
-#include "common.cuh"
+// Design (B200): the ops are HBM-bound, so each row is read from HBM exactly
+// once, kept in registers across the reduction(s), and written once with
+// 16-byte stores.  Rows of up to 512 vectors (4096 bf16) stream through a
+// shared-memory ring filled by 1-D TMA bulk copies (one producer warp, eight
+// consumer warps, one row per consumer at a time, reductions by warp shuffle):
+// the loads in flight are held by the copy engine, not by registers, so a CTA
+// keeps ~96 KB of rows in flight while its warps compute.  Longer rows are
+// owned by a CTA with direct 16-byte loads; shapes that break 16-byte
+// alignment take a scalar block-per-row path.
+#include "pipeline.cuh"
 
 namespace jo {
 namespace {
@@ -98,42 +99,19 @@ __device__ __forceinline__ float norm_elem(float x, float mean, float rstd, floa
   return n;
 }
 
-// ------------------------------------------------------------------ vector path
+// ------------------------------------------------------------------ row math
+// Everything after the row is in registers: (gated residual), reductions,
+// per-element norm/modulation, store or FP8 quantisation.  `raw` holds x (or
+// the residual in kResidGate mode, where `xv` holds x); vector idx = g + i*G.
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp>
-__global__ void __launch_bounds__(kWarp ? 256 : (kVPT <= 4 ? 1024 : (kVPT <= 8 ? 512 : 256)))
-    row_vec_kernel(const RowArgs a) {
+__device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT],
+                                         const uint4 (&xv)[kVPT], int g, int G, float* smem) {
   constexpr int V = Elt<T>::kVec;
-  __shared__ float smem[32];
-  const int G = kWarp ? 32 : blockDim.x;
-  const int g = kWarp ? (threadIdx.x & 31) : threadIdx.x;
-  const int64_t row =
-      kWarp ? (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5) : (int64_t)blockIdx.x;
-  if (row >= a.rows) return;  // uniform per warp (kWarp) or per CTA
   const int nvec = (int)(a.cols / V);
-
-  uint4 raw[kVPT];
-  if constexpr (kPro == kLoadX) {
-    const T* xr = reinterpret_cast<const T*>(a.x) + row * a.x_stride;
-#pragma unroll
-    for (int i = 0; i < kVPT; ++i) {
-      const int idx = g + i * G;
-      if (idx < nvec) raw[i] = ld_stream(xr + (int64_t)idx * V);
-    }
-  } else {
+  if constexpr (kPro == kResidGate) {
     // h = residual + x * gate, rounded to T (the tensor the model materialises)
-    const T* xr = reinterpret_cast<const T*>(a.x) + row * a.x_stride;
-    const T* rr = reinterpret_cast<const T*>(a.res) + row * a.res_stride;
     const T* gr = reinterpret_cast<const T*>(a.gate) + row * a.gate_stride;
     T* hr = reinterpret_cast<T*>(a.out_h) + row * a.h_stride;
-    uint4 xv[kVPT];
-#pragma unroll
-    for (int i = 0; i < kVPT; ++i) {
-      const int idx = g + i * G;
-      if (idx < nvec) {
-        xv[i] = ld_stream(xr + (int64_t)idx * V);
-        raw[i] = ld_stream(rr + (int64_t)idx * V);
-      }
-    }
 #pragma unroll
     for (int i = 0; i < kVPT; ++i) {
       const int idx = g + i * G;
@@ -252,6 +230,110 @@ __global__ void __launch_bounds__(kWarp ? 256 : (kVPT <= 4 ? 1024 : (kVPT <= 8 ?
   }
 }
 
+// ------------------------------------------------------------------ staged path
+// Rows of up to 512 vectors (4096 bf16).  One producer warp keeps a ring of
+// rows in flight with 1-D bulk copies (TMA) into shared memory; kConsumers
+// warps each take every kConsumers-th row of the CTA's contiguous chunk, read
+// it into registers, release the slot at once, and compute + store.  The
+// prefetch depth lives in shared memory, not in registers.
+constexpr int kConsumers = 8;
+constexpr int kStagedThreads = (kConsumers + 1) * 32;
+
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
+__global__ void __launch_bounds__(kStagedThreads, 2)
+    row_staged_kernel(const RowArgs a, int slots, uint32_t slot_bytes, unsigned int* fault) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ float red[32];
+  constexpr int V = Elt<T>::kVec;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t per = (a.rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * per;
+  const int64_t rend = r0 + per < a.rows ? r0 + per : a.rows;
+  const int units = rend > r0 ? (int)(rend - r0) : 0;
+  const int nvec = (int)(a.cols / V);
+  const uint32_t row_bytes = (uint32_t)nvec * 16u;
+  const uint32_t base = smem_u32(smem_raw);
+  Ring ring{base + (uint32_t)(((2 * slots * 8) + 127) & ~127), base, slot_bytes, slots};
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      mbar_init(ring.full(s), 1);
+      mbar_init(ring.empty(s), 1);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (warp == kConsumers) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < units; ++i) {
+        if (!mbar_wait(ring.empty(i), ring.parity(i) ^ 1u, fault)) break;
+        const int64_t row = r0 + i;
+        if constexpr (kPro == kLoadX) {
+          mbar_expect_tx(ring.full(i), row_bytes);
+          bulk_load(ring.slot(i), reinterpret_cast<const T*>(a.x) + row * a.x_stride, row_bytes, ring.full(i));
+        } else {
+          mbar_expect_tx(ring.full(i), 2 * row_bytes);
+          bulk_load(ring.slot(i), reinterpret_cast<const T*>(a.x) + row * a.x_stride, row_bytes, ring.full(i));
+          bulk_load(ring.slot(i) + row_bytes, reinterpret_cast<const T*>(a.res) + row * a.res_stride, row_bytes,
+                    ring.full(i));
+        }
+        issued = i + 1;
+      }
+      // the copies of the last window must land before the CTA may exit
+      for (int i = issued > slots ? issued - slots : 0; i < issued; ++i) mbar_wait(ring.full(i), ring.parity(i), fault);
+    }
+    return;
+  }
+  for (int i = warp; i < units; i += kConsumers) {
+    if (!mbar_wait(ring.full(i), ring.parity(i), fault)) break;
+    uint4 raw[kVPT], xv[kVPT];
+    const uint32_t sl = ring.slot(i);
+#pragma unroll
+    for (int k = 0; k < kVPT; ++k) {
+      const int idx = lane + 32 * k;
+      if (idx < nvec) {
+        if constexpr (kPro == kLoadX) {
+          raw[k] = lds128(sl + idx * 16);
+        } else {
+          xv[k] = lds128(sl + idx * 16);
+          raw[k] = lds128(sl + row_bytes + idx * 16);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ring.empty(i));  // slot free: the row is in registers
+    row_math<T, kVPT, kNorm, kPro, kEpi, true>(a, r0 + i, raw, xv, lane, 32, red);
+  }
+}
+
+// ------------------------------------------------------------------ long rows
+// One CTA per row, loads straight from global memory into registers.
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
+__global__ void __launch_bounds__(kVPT <= 4 ? 1024 : (kVPT <= 8 ? 512 : 256))
+    row_block_kernel(const RowArgs a) {
+  constexpr int V = Elt<T>::kVec;
+  __shared__ float smem[32];
+  const int G = blockDim.x, g = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const int nvec = (int)(a.cols / V);
+  uint4 raw[kVPT], xv[kVPT];
+  const T* xr = reinterpret_cast<const T*>(a.x) + row * a.x_stride;
+  const T* rr = reinterpret_cast<const T*>(a.res) + row * a.res_stride;
+#pragma unroll
+  for (int i = 0; i < kVPT; ++i) {
+    const int idx = g + i * G;
+    if (idx < nvec) {
+      if constexpr (kPro == kLoadX) {
+        raw[i] = ld_stream(xr + (int64_t)idx * V);
+      } else {
+        xv[i] = ld_stream(xr + (int64_t)idx * V);
+        raw[i] = ld_stream(rr + (int64_t)idx * V);
+      }
+    }
+  }
+  row_math<T, kVPT, kNorm, kPro, kEpi, false>(a, row, raw, xv, g, G, smem);
+}
+
 // ------------------------------------------------------------------ scalar path
 // Any alignment, any cols.  One CTA per row; the row is re-read from global
 // memory for each pass (LayerNorm: 3 passes, quant: +1).
@@ -318,12 +400,6 @@ __global__ void __launch_bounds__(256) row_scalar_kernel(const RowArgs a) {
 }
 
 // ------------------------------------------------------------------ dispatch
-template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp>
-int launch_vec(const RowArgs& a, int threads, int64_t grid, cudaStream_t st) {
-  row_vec_kernel<T, kVPT, kNorm, kPro, kEpi, kWarp><<<(unsigned)grid, threads, 0, st>>>(a);
-  return after_launch("row_vec_kernel");
-}
-
 bool row_vec_ok(const RowArgs& a, int esize) {
   const int V = 16 / esize;
   if (a.cols % V) return false;
@@ -338,29 +414,60 @@ bool row_vec_ok(const RowArgs& a, int esize) {
   return true;
 }
 
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
+int launch_staged(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
+  auto kern = row_staged_kernel<T, kVPT, kNorm, kPro, kEpi>;
+  const uint32_t row_bytes = (uint32_t)(a.cols * sizeof(T)) * (kPro == kResidGate ? 2u : 1u);
+  const uint32_t slot_bytes = (row_bytes + 127u) & ~127u;
+  // ~96 KB of ring per CTA (two CTAs per SM), 8..32 slots
+  int slots = (int)((96u * 1024u) / slot_bytes);
+  slots = slots < kConsumers ? kConsumers : (slots > 32 ? 32 : slots);
+  const size_t smem = (size_t)slots * slot_bytes + ((2 * slots * 8 + 127) & ~127);
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+      return fail(JO_ERR_CUDA, "row kernel: cannot reserve shared memory");
+    attr = true;
+  }
+  const int occ = occupancy((const void*)kern, kStagedThreads, smem);
+  int64_t grid = (int64_t)di->sm_count * occ;
+  const int64_t min_rows_per_cta = 4;
+  if (grid * min_rows_per_cta > a.rows) grid = cdiv(a.rows, min_rows_per_cta);
+  if (grid < 1) grid = 1;
+  kern<<<(unsigned)grid, kStagedThreads, smem, st>>>(a, slots, slot_bytes, di->fault);
+  return after_launch("row_staged_kernel");
+}
+
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
+int launch_block(const RowArgs& a, int threads, cudaStream_t st) {
+  row_block_kernel<T, kVPT, kNorm, kPro, kEpi><<<(unsigned)a.rows, threads, 0, st>>>(a);
+  return after_launch("row_block_kernel");
+}
+
 template <typename T, int kNorm, int kPro, int kEpi>
 int launch_rows_t(const RowArgs& a, cudaStream_t st) {
   constexpr int V = Elt<T>::kVec;
   if (a.rows == 0 || a.cols == 0) return JO_OK;
+  const DeviceInfo* di;
+  if (int s = device_info(&di)) return s;
   if (row_vec_ok(a, sizeof(T))) {
-    const int nvec = a.cols / V;
+    const int nvec = (int)(a.cols / V);
     if (nvec <= 32 * 16) {
       const int per = (nvec + 31) / 32;
-      const int64_t grid = cdiv(a.rows, 8);
-#define JO_WARP(VPT) return launch_vec<T, VPT, kNorm, kPro, kEpi, true>(a, 256, grid, st)
-      if (per <= 1) JO_WARP(1);
-      if (per <= 2) JO_WARP(2);
-      if (per <= 4) JO_WARP(4);
-      if (per <= 8) JO_WARP(8);
-      if (per <= 12) JO_WARP(12);
-      JO_WARP(16);
-#undef JO_WARP
+#define JO_STAGED(VPT) return launch_staged<T, VPT, kNorm, kPro, kEpi>(a, st, di)
+      if (per <= 1) JO_STAGED(1);
+      if (per <= 2) JO_STAGED(2);
+      if (per <= 4) JO_STAGED(4);
+      if (per <= 8) JO_STAGED(8);
+      if (per <= 12) JO_STAGED(12);
+      JO_STAGED(16);
+#undef JO_STAGED
     }
     if (nvec <= 256 * 16) {
-#define JO_BLOCK(VPT, MAXTH)                                                                \
-  do {                                                                                      \
-    const int th = (int)(((nvec + VPT - 1) / VPT + 31) / 32 * 32);                          \
-    if (th <= MAXTH) return launch_vec<T, VPT, kNorm, kPro, kEpi, false>(a, th, a.rows, st); \
+#define JO_BLOCK(VPT, MAXTH)                                                                   \
+  do {                                                                                         \
+    const int th = (int)(((nvec + VPT - 1) / VPT + 31) / 32 * 32);                             \
+    if (th <= MAXTH) return launch_block<T, VPT, kNorm, kPro, kEpi>(a, th, st);                \
   } while (0)
       JO_BLOCK(4, 1024);
       JO_BLOCK(8, 512);

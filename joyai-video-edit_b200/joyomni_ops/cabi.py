@@ -42,6 +42,7 @@ SIGNATURES = {
     "jo_status_name": [I32],
     "jo_last_error": [],
     "jo_launch_count": [],
+    "jo_device_fault_count": [C.POINTER(C.c_uint32)],
     "jo_rmsnorm": [P, I64, P, I64, P, I64, I64, I32, F32, P],
     "jo_norm_scale_shift": [P, I64, P, I64, P, P, P, P, I64, I64, I64, I64, I32, I32, F32, P],
     "jo_qk_norm_rope_3d_paired": [P, P, I64, I64, I64, I64, F32, P, P, P, P, P, P],
@@ -97,6 +98,13 @@ def status_of(name: str, *args) -> int:
 
 def launch_count() -> int:
     return int(lib().jo_launch_count())
+
+
+def device_fault_count() -> int:
+    """Bounded-wait expiries recorded on the current device since the last call."""
+    n = C.c_uint32(0)
+    call("jo_device_fault_count", C.byref(n))
+    return int(n.value)
 
 
 # ------------------------------------------------------------------ torch helpers

@@ -85,6 +85,7 @@ def assert_bf16_close(out: torch.Tensor, ref: torch.Tensor, max_ulp: float = 1.0
 
 
 MANTISSA_BITS = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}
+MIN_ULP = {torch.bfloat16: 2.0 ** -133, torch.float16: 2.0 ** -24, torch.float32: 2.0 ** -149}
 
 
 def assert_ulp_close(out: torch.Tensor, ref: torch.Tensor, max_ulp: float = 1.0, floor: float = 2.0 ** -10,
@@ -102,7 +103,8 @@ def assert_ulp_close(out: torch.Tensor, ref: torch.Tensor, max_ulp: float = 1.0,
         return 1.0
     assert torch.isfinite(o).all(), f"{what}: non-finite output"
     mag = r.abs().clamp_min(floor)
-    ulp = torch.pow(2.0, torch.floor(torch.log2(mag)) - bits)
+    # ulp of the value, never below the dtype's subnormal spacing
+    ulp = torch.pow(2.0, torch.floor(torch.log2(mag)) - bits).clamp_min(MIN_ULP[ref.dtype])
     allowed = max_ulp * ulp + (atol.float().cpu() if atol is not None else 0.0)
     bad = (o - r).abs() > allowed
     if bad.any():

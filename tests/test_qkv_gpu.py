@@ -153,8 +153,12 @@ def test_joint_qkv_pack(jo, dev, img_len, txt_len, cache_len, heads, odd):
     n = img_len * 1
     assert torch.equal(oq.cpu()[:, :n], rq[:, :n])
     assert torch.equal(ok.cpu()[:, : cache_len + n], rk[:, : cache_len + n])
-    assert_ulp_close(oq, rq, 1.0, what="q")
-    assert_ulp_close(ok, rk, 1.0, what="k")
+    # text rows: the model's double rounding (bf16(x*r), then bf16(. * w)) turns a
+    # 1-ulp flip of the first rounding (r differs from torch's in the last fp32
+    # bits) into |w| ulps of the output; w ~ N(0, 1) as in the reference test
+    fq = assert_ulp_close(oq, rq, 4.0, what="q")
+    fk = assert_ulp_close(ok, rk, 4.0, what="k")
+    assert fq > 0.99 and fk > 0.99
 
 
 @pytest.mark.parametrize("len0,len1,heads", [(13, 7, 4), (13, 0, 4), (4000, 1200, 24)])

@@ -2,7 +2,8 @@
 
 bf16/fp16 outputs: <= 1 ulp of the oracle value (ulp taken at max(|ref|, 2^-10)
 so cancellation to tiny values is judged against the O(1) terms); fp32
-outputs: <= 64 fp32 ulps (reduction order).  FP8 bytes and scales: bit-exact.
+outputs: <= 64 fp32 ulps of max(|ref|, 0.25) (reduction order; the modulated
+terms are O(1) and cancel).  FP8 bytes and scales: bit-exact.
 """
 import pytest
 import torch
@@ -20,6 +21,10 @@ def ulps(dt):
     return 64.0 if dt == torch.float32 else 1.0
 
 
+def floor_for(dt):
+    return 0.25 if dt == torch.float32 else 2.0 ** -10
+
+
 def rand(shape, dt, seed, scale=1.0, mean=0.0):
     g = torch.Generator().manual_seed(seed)
     return (mean + scale * torch.randn(*shape, generator=g)).to(dt)
@@ -32,7 +37,7 @@ def test_rmsnorm(jo, dev, dt, shape):
     x = rand(shape, dt, 1)
     w = rand((N,), dt, 2, 0.02, 1.0)
     out = jo.rmsnorm(x.to(dev), w.to(dev), 1e-6)
-    assert_ulp_close(out, ops.rmsnorm(x, w, 1e-6), ulps(dt), what=f"rmsnorm {dt} {shape}")
+    assert_ulp_close(out, ops.rmsnorm(x, w, 1e-6), ulps(dt), floor_for(dt), what=f"rmsnorm {dt} {shape}")
 
 
 def test_rmsnorm_cabi_strided_guarded(cabi, dev):
@@ -66,7 +71,7 @@ def test_norm_scale_shift(jo, dev, dt, norm, per_row, affine, shape):
     g = lambda t: t.to(dev) if t is not None else None
     out = jo.fused_norm_scale_shift(g(x), g(gamma), g(beta), g(scale), g(shift), norm, 1e-6)
     ref = ops.norm_scale_shift(x, gamma, beta, scale, shift, norm, 1e-6)
-    assert_ulp_close(out, ref, ulps(dt), what=f"norm_scale_shift {norm} {dt} {shape}")
+    assert_ulp_close(out, ref, ulps(dt), floor_for(dt), what=f"norm_scale_shift {norm} {dt} {shape}")
 
 
 def test_norm_scale_shift_rejects(jo, dev):
@@ -135,20 +140,33 @@ def test_per_token_quant_bit_exact(jo, dev, dt, shape):
 
 
 def test_per_token_quant_reference_assert(jo, dev):
-    # joyomni_ops/tests/test_parity_light.py:113-133, asserted the same way
+    """joyomni_ops/tests/test_parity_light.py:113-133, asserted the same way.
+
+    The reference formula is evaluated on the CPU (the oracle).  Evaluated with
+    torch on the GPU instead, the same formula differs from its own CPU result
+    in a few rounding-boundary elements, so that comparison is looser.
+    """
     M, N = 67, 4096
     x = torch.randn(M, N, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
     x[0].zero_()
     q = torch.empty(M, N, dtype=torch.float8_e4m3fn, device=dev)
     scale = torch.empty((M, 1), device=dev, dtype=torch.float32)
     jo.sgl_per_token_quant_fp8(x.to(dev), q, scale)
-    xg = x.to(dev)
-    ref_scale = xg.abs().amax(dim=1, keepdim=True).float().clamp_min(1e-8) / 448.0
-    ref_q = (xg.float() / ref_scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
-    scale_rel = ((scale - ref_scale).abs().max() / ref_scale.abs().max().clamp_min(1e-9)).item()
-    q_rel = ((q.float() * scale - ref_q.float() * ref_scale).abs().mean()
-             / (ref_q.float() * ref_scale).abs().mean().clamp_min(1e-9)).item()
-    assert scale_rel < 1e-5 and q_rel < 1e-5
+    q, scale = q.cpu(), scale.cpu()
+
+    def rel(xr):
+        ref_scale = xr.abs().amax(dim=1, keepdim=True).float().clamp_min(1e-8) / 448.0
+        ref_q = (xr.float() / ref_scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+        ref_scale, ref_q = ref_scale.cpu(), ref_q.cpu()
+        scale_rel = ((scale - ref_scale).abs().max() / ref_scale.abs().max().clamp_min(1e-9)).item()
+        q_rel = ((q.float() * scale - ref_q.float() * ref_scale).abs().mean()
+                 / (ref_q.float() * ref_scale).abs().mean().clamp_min(1e-9)).item()
+        return scale_rel, q_rel
+
+    s_rel, q_rel = rel(x)
+    assert s_rel == 0.0 and q_rel == 0.0  # bit-exact to the CPU reference formula
+    s_rel, q_rel = rel(x.to(dev))
+    assert s_rel < 1e-5 and q_rel < 1e-4
 
 
 @pytest.mark.parametrize("shape", [(10800, 3072), (40, 4096), (3, 136), (2, 12288)])
