@@ -14,7 +14,7 @@
 // issued before the first use); grids are sized to the resident-CTA capacity
 // of the 148 SMs and walk the rows with a grid-stride loop.  Destination
 // rows are 2*D contiguous bytes, so every store fills whole 32-byte sectors.
-#include "common.cuh"
+#include "pipeline.cuh"
 
 namespace jo {
 namespace {
@@ -174,6 +174,150 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Staged variant (B200 fast path).  Unit = all heads of one token for one of
+// q/k/v (kPack: a contiguous H*D slice of the qkv row) or for q/k (kInPlace: a
+// contiguous token row of q or k).  One producer lane streams units into a
+// shared-memory ring with 1-D bulk copies; kQkConsumers warps each take every
+// kQkConsumers-th unit, normalise + rotate head rows straight out of shared
+// memory (D/8 lanes per head, 16 bytes per lane) and store 2*D-byte rows.
+constexpr int kQkConsumers = 16;
+constexpr int kQkThreads = (kQkConsumers + 1) * 32;
+
+template <int kD, int kMode, bool kPre>
+__global__ void __launch_bounds__(kQkThreads, 1)
+    qk_staged_kernel(const QkArgs a, int tok_per_cta, int slots, uint32_t slot_bytes, unsigned int* fault) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  constexpr int kTPH = kD / 8;
+  constexpr int kHPI = 32 / kTPH;  // heads per warp iteration
+  constexpr int kParts = kMode == kPack ? 3 : 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = lane % kTPH, sub = lane / kTPH;
+  const int H = (int)a.heads;
+  const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * H);  // tokens (kInPlace: batch*seq rows)
+  const int64_t t0 = (int64_t)blockIdx.x * tok_per_cta;
+  const int64_t t1 = t0 + tok_per_cta < ntok ? t0 + tok_per_cta : ntok;
+  const int units = t1 > t0 ? (int)(t1 - t0) * kParts : 0;
+  const uint32_t unit_bytes = (uint32_t)H * kD * 2u;
+  const uint32_t base = smem_u32(smem_raw);
+  Ring ring{base + (uint32_t)(((2 * slots * 8) + 127) & ~127), base, slot_bytes, slots};
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      mbar_init(ring.full(s), 1);
+      mbar_init(ring.empty(s), 1);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  auto unit_src = [&](int i, int64_t& tok, int& part) -> const __nv_bfloat16* {
+    tok = t0 + i / kParts;
+    part = i % kParts;
+    if constexpr (kMode == kPack)
+      return a.qkv + tok * a.qkv_stride + (int64_t)part * H * kD;
+    else
+      return (part ? a.k : a.q) + tok * (int64_t)H * kD;
+  };
+  if (warp == kQkConsumers) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < units; ++i) {
+        if (!mbar_wait(ring.empty(i), ring.parity(i) ^ 1u, fault)) break;
+        int64_t tok;
+        int part;
+        const __nv_bfloat16* src = unit_src(i, tok, part);
+        mbar_expect_tx(ring.full(i), unit_bytes);
+        bulk_load(ring.slot(i), src, unit_bytes, ring.full(i));
+        issued = i + 1;
+      }
+      for (int i = issued > slots ? issued - slots : 0; i < issued; ++i) mbar_wait(ring.full(i), ring.parity(i), fault);
+    }
+    return;
+  }
+  float wq[8], wk[8];
+  Elt<__nv_bfloat16>::unpack(ld_bcast(a.qw + j * 8), wq);
+  Elt<__nv_bfloat16>::unpack(ld_bcast(a.kw + j * 8), wk);
+  const float inv_d = 1.0f / (float)kD;
+  for (int i = warp; i < units; i += kQkConsumers) {
+    int64_t tok;
+    int part;
+    __nv_bfloat16* dst_unit = const_cast<__nv_bfloat16*>(unit_src(i, tok, part));  // kInPlace destination
+    const int64_t rope_tok = kMode == kPack ? tok : tok % a.seq_len;
+    float c[4], sn[4];
+    if (part < 2) {
+      const int64_t co = rope_tok * (kD / 2) + j * 4;
+      unpack_bf16x4(__ldg(reinterpret_cast<const uint2*>(a.cos + co)), c);
+      unpack_bf16x4(__ldg(reinterpret_cast<const uint2*>(a.sin + co)), sn);
+    }
+    if (!mbar_wait(ring.full(i), ring.parity(i), fault)) break;
+    const uint32_t sl = ring.slot(i);
+    for (int h0 = 0; h0 < H; h0 += kHPI) {
+      const int h = h0 + sub;
+      const bool ok = h < H;
+      const uint4 v = ok ? lds128(sl + (uint32_t)(h * kD + j * 8) * 2u) : make_uint4(0, 0, 0, 0);
+      float f[8];
+      Elt<__nv_bfloat16>::unpack(v, f);
+      const float ss = head_sumsq<kTPH>(f);  // every lane, before any divergence
+      if (!ok) continue;
+      int64_t dst_off;
+      __nv_bfloat16* dst;
+      if constexpr (kMode == kPack) {
+        dst_off = (int64_t)h * a.os_h + tok * a.os_t + j * 8;
+        dst = part == 0 ? a.out[0] : (part == 1 ? a.out[1] : a.out[2]);
+      } else {
+        dst_off = (int64_t)h * kD + j * 8;
+        dst = dst_unit;
+      }
+      if (part == 2) {
+        st_global(dst + dst_off, v);
+        continue;
+      }
+      head_scale(f, part == 0 ? wq : wk, ss, inv_d, a.eps);
+      if constexpr (kPre) {
+        if (part == 1) {
+          const int64_t pre_off = kMode == kPack ? dst_off : tok * (int64_t)H * kD + dst_off;
+          st_global(a.k_pre + pre_off, Elt<__nv_bfloat16>::pack(f));
+        }
+      }
+      rope4(f, c, sn);
+      st_global(dst + dst_off, Elt<__nv_bfloat16>::pack(f));
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ring.empty(i));
+  }
+}
+
+template <int kD, int kMode, bool kPre>
+int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, bool& taken) {
+  constexpr int kParts = kMode == kPack ? 3 : 2;
+  taken = false;
+  const uint32_t unit_bytes = a.heads * kD * 2u;
+  const uint32_t slot_bytes = (unit_bytes + 127u) & ~127u;
+  // slot count a multiple of the consumer count: each slot belongs to one
+  // consumer warp, so no warp can wait on a slot more than one phase ahead
+  int slots = (int)((192u * 1024u) / slot_bytes) / kQkConsumers * kQkConsumers;
+  if (slots < kQkConsumers) return JO_OK;  // units too large to stage: caller uses the direct path
+  if (slots > 4 * kQkConsumers) slots = 4 * kQkConsumers;
+  taken = true;
+  auto kern = qk_staged_kernel<kD, kMode, kPre>;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
+      return fail(JO_ERR_CUDA, "qk kernel: cannot reserve shared memory");
+    attr = true;
+  }
+  const size_t smem = (size_t)slots * slot_bytes + ((2 * slots * 8 + 127) & ~127);
+  const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * a.heads);
+  int64_t grid = di->sm_count;
+  int64_t per = cdiv(ntok, grid);
+  if (per < 4) {  // small problems: fewer CTAs with a few tokens each
+    per = 4;
+    grid = cdiv(ntok, per);
+  }
+  grid = cdiv(ntok, per);
+  kern<<<(unsigned)grid, kQkThreads, smem, st>>>(a, (int)per, slots, slot_bytes, di->fault);
+  return after_launch("qk_staged_kernel");
+}
+
 template <int kD, int kMode, bool kPre>
 int launch_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
   auto kern = qk_norm_rope_kernel<kD, kMode, kPre>;
@@ -188,13 +332,21 @@ int launch_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
   return after_launch("qk_norm_rope_kernel");
 }
 
+template <int kD, int kMode, bool kPre>
+int run_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
+  bool taken = false;
+  const int s = launch_qk_staged<kD, kMode, kPre>(a, st, di, taken);
+  if (taken) return s;
+  return launch_qk<kD, kMode, kPre>(a, st, di);
+}
+
 template <int kMode>
 int dispatch_qk(int64_t head_dim, bool pre, const QkArgs& a, cudaStream_t st,
                 const DeviceInfo* di) {
   switch (head_dim) {
-    case 64: return pre ? launch_qk<64, kMode, true>(a, st, di) : launch_qk<64, kMode, false>(a, st, di);
-    case 128: return pre ? launch_qk<128, kMode, true>(a, st, di) : launch_qk<128, kMode, false>(a, st, di);
-    case 256: return pre ? launch_qk<256, kMode, true>(a, st, di) : launch_qk<256, kMode, false>(a, st, di);
+    case 64: return pre ? run_qk<64, kMode, true>(a, st, di) : run_qk<64, kMode, false>(a, st, di);
+    case 128: return pre ? run_qk<128, kMode, true>(a, st, di) : run_qk<128, kMode, false>(a, st, di);
+    case 256: return pre ? run_qk<256, kMode, true>(a, st, di) : run_qk<256, kMode, false>(a, st, di);
     default: return fail(JO_ERR_SHAPE, "head_dim must be 64, 128 or 256, got %lld", (long long)head_dim);
   }
 }

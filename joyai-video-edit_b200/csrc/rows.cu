@@ -13,8 +13,8 @@
 // 16-byte stores.  Rows of up to 512 vectors (4096 bf16) stream through a
 // shared-memory ring filled by 1-D TMA bulk copies (one producer warp, eight
 // consumer warps, one row per consumer at a time, reductions by warp shuffle):
-// the loads in flight are held by the copy engine, not by registers, so a CTA
-// keeps ~96 KB of rows in flight while its warps compute.  Longer rows are
+// the loads in flight are held by the copy engine, not by registers, so each
+// SM keeps ~192 KB of rows in flight while its warps compute.  Longer rows are
 // owned by a CTA with direct 16-byte loads; shapes that break 16-byte
 // alignment take a scalar block-per-row path.
 #include "pipeline.cuh"
@@ -103,28 +103,35 @@ __device__ __forceinline__ float norm_elem(float x, float mean, float rstd, floa
 // Everything after the row is in registers: (gated residual), reductions,
 // per-element norm/modulation, store or FP8 quantisation.  `raw` holds x (or
 // the residual in kResidGate mode, where `xv` holds x); vector idx = g + i*G.
-template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp>
+// h = residual + x * gate for one vector, rounded to T (the tensor the model
+// materialises), and written to out_h.
+template <typename T>
+__device__ __forceinline__ uint4 resid_vec(const RowArgs& a, int64_t row, int idx, const uint4& xv,
+                                           const uint4& rv) {
+  constexpr int V = Elt<T>::kVec;
+  const T* gr = reinterpret_cast<const T*>(a.gate) + row * a.gate_stride;
+  float fx[V], fr[V], fg[V], fh[V];
+  Elt<T>::unpack(xv, fx);
+  Elt<T>::unpack(rv, fr);
+  Elt<T>::unpack(ld_bcast(gr + (int64_t)idx * V), fg);
+#pragma unroll
+  for (int j = 0; j < V; ++j) fh[j] = fr[j] + fx[j] * fg[j];
+  const uint4 h = Elt<T>::pack(fh);
+  st_global(reinterpret_cast<T*>(a.out_h) + row * a.h_stride + (int64_t)idx * V, h);
+  return h;
+}
+
+// kHDone: the caller already formed h (kResidGate) into raw and stored it.
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp, bool kHDone = false>
 __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT],
                                          const uint4 (&xv)[kVPT], int g, int G, float* smem) {
   constexpr int V = Elt<T>::kVec;
   const int nvec = (int)(a.cols / V);
-  if constexpr (kPro == kResidGate) {
-    // h = residual + x * gate, rounded to T (the tensor the model materialises)
-    const T* gr = reinterpret_cast<const T*>(a.gate) + row * a.gate_stride;
-    T* hr = reinterpret_cast<T*>(a.out_h) + row * a.h_stride;
+  if constexpr (kPro == kResidGate && !kHDone) {
 #pragma unroll
     for (int i = 0; i < kVPT; ++i) {
       const int idx = g + i * G;
-      if (idx < nvec) {
-        float fx[V], fr[V], fg[V], fh[V];
-        Elt<T>::unpack(xv[i], fx);
-        Elt<T>::unpack(raw[i], fr);
-        Elt<T>::unpack(ld_bcast(gr + (int64_t)idx * V), fg);
-#pragma unroll
-        for (int j = 0; j < V; ++j) fh[j] = fr[j] + fx[j] * fg[j];
-        raw[i] = Elt<T>::pack(fh);
-        st_global(hr + (int64_t)idx * V, raw[i]);
-      }
+      if (idx < nvec) raw[i] = resid_vec<T>(a, row, idx, xv[i], raw[i]);
     }
   }
   if constexpr (kEpi == kNoY) return;
@@ -235,12 +242,12 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
 // rows in flight with 1-D bulk copies (TMA) into shared memory; kConsumers
 // warps each take every kConsumers-th row of the CTA's contiguous chunk, read
 // it into registers, release the slot at once, and compute + store.  The
-// prefetch depth lives in shared memory, not in registers.
-constexpr int kConsumers = 8;
+// prefetch depth lives in shared memory, not in registers.  One CTA per SM.
+constexpr int kConsumers = 12;
 constexpr int kStagedThreads = (kConsumers + 1) * 32;
 
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
-__global__ void __launch_bounds__(kStagedThreads, 2)
+__global__ void __launch_bounds__(kStagedThreads, 1)
     row_staged_kernel(const RowArgs a, int slots, uint32_t slot_bytes, unsigned int* fault) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ float red[32];
@@ -286,23 +293,21 @@ __global__ void __launch_bounds__(kStagedThreads, 2)
   }
   for (int i = warp; i < units; i += kConsumers) {
     if (!mbar_wait(ring.full(i), ring.parity(i), fault)) break;
-    uint4 raw[kVPT], xv[kVPT];
+    uint4 raw[kVPT];
     const uint32_t sl = ring.slot(i);
 #pragma unroll
     for (int k = 0; k < kVPT; ++k) {
       const int idx = lane + 32 * k;
       if (idx < nvec) {
-        if constexpr (kPro == kLoadX) {
+        if constexpr (kPro == kLoadX)
           raw[k] = lds128(sl + idx * 16);
-        } else {
-          xv[k] = lds128(sl + idx * 16);
-          raw[k] = lds128(sl + row_bytes + idx * 16);
-        }
+        else  // form h = residual + x * gate straight from the slot
+          raw[k] = resid_vec<T>(a, r0 + i, idx, lds128(sl + idx * 16), lds128(sl + row_bytes + idx * 16));
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(ring.empty(i));  // slot free: the row is in registers
-    row_math<T, kVPT, kNorm, kPro, kEpi, true>(a, r0 + i, raw, xv, lane, 32, red);
+    row_math<T, kVPT, kNorm, kPro, kEpi, true, true>(a, r0 + i, raw, raw, lane, 32, red);
   }
 }
 
@@ -419,13 +424,17 @@ int launch_staged(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   auto kern = row_staged_kernel<T, kVPT, kNorm, kPro, kEpi>;
   const uint32_t row_bytes = (uint32_t)(a.cols * sizeof(T)) * (kPro == kResidGate ? 2u : 1u);
   const uint32_t slot_bytes = (row_bytes + 127u) & ~127u;
-  // ~96 KB of ring per CTA (two CTAs per SM), 8..32 slots
-  int slots = (int)((96u * 1024u) / slot_bytes);
-  slots = slots < kConsumers ? kConsumers : (slots > 32 ? 32 : slots);
+  // ~192 KB of ring per CTA (one CTA per SM).  The slot count is a multiple of
+  // kConsumers so that every slot is only ever used by one consumer warp (unit
+  // i -> warp i % kConsumers, slot i % slots): a warp then never waits on a
+  // slot more than one phase ahead, which a parity wait could not tell apart.
+  int slots = (int)((192u * 1024u) / slot_bytes) / kConsumers * kConsumers;
+  if (slots < kConsumers) slots = kConsumers;
+  if (slots > 4 * kConsumers) slots = 4 * kConsumers;
   const size_t smem = (size_t)slots * slot_bytes + ((2 * slots * 8 + 127) & ~127);
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
       return fail(JO_ERR_CUDA, "row kernel: cannot reserve shared memory");
     attr = true;
   }
