@@ -36,7 +36,8 @@ NVCC_FLAGS = ARCH + [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CU_SOURCES = ["common.cu", "rows.cu", "qkv.cu", "elementwise.cu", "fp8_gemm.cu"]
+CU_SOURCES = ["common.cu", "rows.cu", "rows_bf16.cu", "rows_f16.cu", "rows_f32.cu", "qkv.cu", "elementwise.cu",
+              "fp8_gemm.cu"]
 LIB = OUT / "libjoyomni_b200.so"
 SHIM = OUT / "_C.so"
 

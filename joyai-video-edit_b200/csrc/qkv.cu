@@ -177,16 +177,23 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
 // ---------------------------------------------------------------------------
 // Staged variant (B200 fast path).  Unit = all heads of one token for one of
 // q/k/v (kPack: a contiguous H*D slice of the qkv row) or for q/k (kInPlace: a
-// contiguous token row of q or k).  One producer lane streams units into a
-// shared-memory ring with 1-D bulk copies; kQkConsumers warps each take every
-// kQkConsumers-th unit, normalise + rotate head rows straight out of shared
-// memory (D/8 lanes per head, 16 bytes per lane) and store 2*D-byte rows.
-constexpr int kQkConsumers = 16;
-constexpr int kQkThreads = (kQkConsumers + 1) * 32;
+// contiguous token row of q or k).  Each warp owns kQkSlots shared-memory
+// slots and feeds itself with 1-D TMA bulk copies: when a unit lands the warp
+// pulls it into registers (D/8 lanes per head, 16 bytes per lane), refills the
+// slot with its unit kQkSlots ahead, then normalises + rotates with packed
+// fp32 (f32x2) arithmetic and stores 2*D-byte rows.  The head rsqrt uses the
+// hardware approximation (rel. error ~2^-22, far below the bf16 output ulp).
+constexpr int kQkWarps = 16;
+constexpr int kQkSlots = 2;
+constexpr int kQkMaxIt = 16;  // head iterations held in registers (H <= 16 * 32/(D/8))
+
+__device__ __forceinline__ float2 bf2f(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
 
 template <int kD, int kMode, bool kPre>
-__global__ void __launch_bounds__(kQkThreads, 1)
-    qk_staged_kernel(const QkArgs a, int tok_per_cta, int slots, uint32_t slot_bytes, unsigned int* fault) {
+__global__ void __launch_bounds__(kQkWarps * 32, 1)
+    qk_staged_kernel(const QkArgs a, int tok_per_cta, uint32_t slot_bytes, unsigned int* fault) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   constexpr int kTPH = kD / 8;
   constexpr int kHPI = 32 / kTPH;  // heads per warp iteration
@@ -194,109 +201,165 @@ __global__ void __launch_bounds__(kQkThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int j = lane % kTPH, sub = lane / kTPH;
   const int H = (int)a.heads;
-  const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * H);  // tokens (kInPlace: batch*seq rows)
+  const int NI = (H + kHPI - 1) / kHPI;
+  const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * H);
   const int64_t t0 = (int64_t)blockIdx.x * tok_per_cta;
   const int64_t t1 = t0 + tok_per_cta < ntok ? t0 + tok_per_cta : ntok;
   const int units = t1 > t0 ? (int)(t1 - t0) * kParts : 0;
   const uint32_t unit_bytes = (uint32_t)H * kD * 2u;
   const uint32_t base = smem_u32(smem_raw);
-  Ring ring{base + (uint32_t)(((2 * slots * 8) + 127) & ~127), base, slot_bytes, slots};
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < slots; ++s) {
-      mbar_init(ring.full(s), 1);
-      mbar_init(ring.empty(s), 1);
-    }
-    mbar_init_fence();
-  }
+  if (threadIdx.x < kQkWarps * kQkSlots) mbar_init(base + 8u * threadIdx.x, 1);
+  if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
-  auto unit_src = [&](int i, int64_t& tok, int& part) -> const __nv_bfloat16* {
+  const uint32_t bar0 = base + 8u * (uint32_t)(warp * kQkSlots);
+  const uint32_t slot0 = base + 256u + (uint32_t)(warp * kQkSlots) * slot_bytes;
+  auto unit_ptr = [&](int i, int64_t& tok, int& part) -> __nv_bfloat16* {
     tok = t0 + i / kParts;
     part = i % kParts;
     if constexpr (kMode == kPack)
-      return a.qkv + tok * a.qkv_stride + (int64_t)part * H * kD;
+      return const_cast<__nv_bfloat16*>(a.qkv) + tok * a.qkv_stride + (int64_t)part * H * kD;
     else
       return (part ? a.k : a.q) + tok * (int64_t)H * kD;
   };
-  if (warp == kQkConsumers) {
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < units; ++i) {
-        if (!mbar_wait(ring.empty(i), ring.parity(i) ^ 1u, fault)) break;
-        int64_t tok;
-        int part;
-        const __nv_bfloat16* src = unit_src(i, tok, part);
-        mbar_expect_tx(ring.full(i), unit_bytes);
-        bulk_load(ring.slot(i), src, unit_bytes, ring.full(i));
-        issued = i + 1;
-      }
-      for (int i = issued > slots ? issued - slots : 0; i < issued; ++i) mbar_wait(ring.full(i), ring.parity(i), fault);
-    }
-    return;
-  }
-  float wq[8], wk[8];
-  Elt<__nv_bfloat16>::unpack(ld_bcast(a.qw + j * 8), wq);
-  Elt<__nv_bfloat16>::unpack(ld_bcast(a.kw + j * 8), wk);
-  const float inv_d = 1.0f / (float)kD;
-  for (int i = warp; i < units; i += kQkConsumers) {
+  // unit kk of this warp is unit warp + kk * kQkWarps of the CTA, slot kk % kQkSlots
+  auto issue = [&](int kk) {
+    const int i = warp + kk * kQkWarps;
+    if (i >= units) return;
     int64_t tok;
     int part;
-    __nv_bfloat16* dst_unit = const_cast<__nv_bfloat16*>(unit_src(i, tok, part));  // kInPlace destination
-    const int64_t rope_tok = kMode == kPack ? tok : tok % a.seq_len;
-    float c[4], sn[4];
-    if (part < 2) {
-      const int64_t co = rope_tok * (kD / 2) + j * 4;
-      unpack_bf16x4(__ldg(reinterpret_cast<const uint2*>(a.cos + co)), c);
-      unpack_bf16x4(__ldg(reinterpret_cast<const uint2*>(a.sin + co)), sn);
+    const __nv_bfloat16* src = unit_ptr(i, tok, part);
+    const uint32_t bar = bar0 + 8u * (uint32_t)(kk % kQkSlots);
+    mbar_expect_tx(bar, unit_bytes);
+    bulk_load(slot0 + (uint32_t)(kk % kQkSlots) * slot_bytes, src, unit_bytes, bar);
+  };
+  if (lane == 0)
+    for (int kk = 0; kk < kQkSlots; ++kk) issue(kk);
+  float2 wq[4], wk[4];
+  {
+    const uint4 q4 = ld_bcast(a.qw + j * 8), k4 = ld_bcast(a.kw + j * 8);
+    const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w}, kw[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      wq[e] = bf2f(qw[e]);
+      wk[e] = bf2f(kw[e]);
     }
-    if (!mbar_wait(ring.full(i), ring.parity(i), fault)) break;
-    const uint32_t sl = ring.slot(i);
-    for (int h0 = 0; h0 < H; h0 += kHPI) {
-      const int h = h0 + sub;
-      const bool ok = h < H;
-      const uint4 v = ok ? lds128(sl + (uint32_t)(h * kD + j * 8) * 2u) : make_uint4(0, 0, 0, 0);
-      float f[8];
-      Elt<__nv_bfloat16>::unpack(v, f);
-      const float ss = head_sumsq<kTPH>(f);  // every lane, before any divergence
-      if (!ok) continue;
-      int64_t dst_off;
-      __nv_bfloat16* dst;
-      if constexpr (kMode == kPack) {
-        dst_off = (int64_t)h * a.os_h + tok * a.os_t + j * 8;
-        dst = part == 0 ? a.out[0] : (part == 1 ? a.out[1] : a.out[2]);
-      } else {
-        dst_off = (int64_t)h * kD + j * 8;
-        dst = dst_unit;
+  }
+  const float inv_d = 1.0f / (float)kD;  // exact for power-of-two D
+  int kk = 0;
+  for (; warp + kk * kQkWarps < units; ++kk) {
+    const int i = warp + kk * kQkWarps;
+    int64_t tok;
+    int part;
+    __nv_bfloat16* unit_dst = unit_ptr(i, tok, part);  // kInPlace destination
+    float2 cs[4], ns[4];  // (c, s) and (-s, c) per rotated pair
+    if (part < 2) {
+      const int64_t rt = kMode == kPack ? tok : tok % a.seq_len;
+      const uint2 c2 = __ldg(reinterpret_cast<const uint2*>(a.cos + rt * (kD / 2) + j * 4));
+      const uint2 s2 = __ldg(reinterpret_cast<const uint2*>(a.sin + rt * (kD / 2) + j * 4));
+      const float2 c01 = bf2f(c2.x), c23 = bf2f(c2.y), s01 = bf2f(s2.x), s23 = bf2f(s2.y);
+      const float c[4] = {c01.x, c01.y, c23.x, c23.y}, sn[4] = {s01.x, s01.y, s23.x, s23.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        cs[e] = make_float2(c[e], sn[e]);
+        ns[e] = make_float2(-sn[e], c[e]);
       }
-      if (part == 2) {
-        st_global(dst + dst_off, v);
-        continue;
-      }
-      head_scale(f, part == 0 ? wq : wk, ss, inv_d, a.eps);
-      if constexpr (kPre) {
-        if (part == 1) {
-          const int64_t pre_off = kMode == kPack ? dst_off : tok * (int64_t)H * kD + dst_off;
-          st_global(a.k_pre + pre_off, Elt<__nv_bfloat16>::pack(f));
-        }
-      }
-      rope4(f, c, sn);
-      st_global(dst + dst_off, Elt<__nv_bfloat16>::pack(f));
+    }
+    const uint32_t bar = bar0 + 8u * (uint32_t)(kk % kQkSlots);
+    const uint32_t sl = slot0 + (uint32_t)(kk % kQkSlots) * slot_bytes;
+    if (!mbar_wait(bar, (uint32_t)((kk / kQkSlots) & 1), fault)) break;
+    uint4 v[kQkMaxIt];
+#pragma unroll
+    for (int it = 0; it < kQkMaxIt; ++it) {
+      const int h = it * kHPI + sub;
+      v[it] = (it < NI && h < H) ? lds128(sl + (uint32_t)(h * kD + j * 8) * 2u) : make_uint4(0, 0, 0, 0);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(ring.empty(i));
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // reads before the refill
+      issue(kk + kQkSlots);
+    }
+    const float2* w = part == 0 ? wq : wk;
+    // groups of 4 head iterations, phase-major, so the 4 shuffle + rsqrt
+    // dependency chains of a group overlap
+#pragma unroll
+    for (int g0 = 0; g0 < kQkMaxIt; g0 += 4) {
+      if (g0 >= NI) break;  // uniform across the warp
+      float ss[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = v[g0 + q];
+        float2 p0 = bf2f(u.x), p1 = bf2f(u.y), p2 = bf2f(u.z), p3 = bf2f(u.w);
+        float2 acc = __fmul2_rn(p0, p0);
+        acc = __ffma2_rn(p1, p1, acc);
+        acc = __ffma2_rn(p2, p2, acc);
+        acc = __ffma2_rn(p3, p3, acc);
+        ss[q] = (g0 + q < NI) ? acc.x + acc.y : 0.f;
+      }
+#pragma unroll
+      for (int o = kTPH / 2; o > 0; o >>= 1)  // every lane, before any divergence
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ss[q] += __shfl_xor_sync(0xffffffffu, ss[q], o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int it = g0 + q;
+        const int h = it * kHPI + sub;
+        if (it >= NI || h >= H) continue;
+        int64_t off;
+        __nv_bfloat16* dst;
+        if constexpr (kMode == kPack) {
+          off = (int64_t)h * a.os_h + tok * a.os_t + j * 8;
+          dst = part == 0 ? a.out[0] : (part == 1 ? a.out[1] : a.out[2]);
+        } else {
+          off = (int64_t)h * kD + j * 8;
+          dst = unit_dst;
+        }
+        if (part == 2) {
+          st_global(dst + off, v[it]);
+          continue;
+        }
+        const uint32_t u[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+        float2 p[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[e] = bf2f(u[e]);
+        const float r = rsqrtf(fmaf(ss[q], inv_d, a.eps));
+        const float2 r2 = make_float2(r, r);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[e] = __fmul2_rn(__fmul2_rn(p[e], r2), w[e]);  // (x * r) * w
+        if constexpr (kPre) {
+          if (part == 1) {
+            const int64_t pre = kMode == kPack ? off : tok * (int64_t)H * kD + off;
+            st_global(a.k_pre + pre, make_uint4(pack_bf16x2(p[0].x, p[0].y), pack_bf16x2(p[1].x, p[1].y),
+                                                pack_bf16x2(p[2].x, p[2].y), pack_bf16x2(p[3].x, p[3].y)));
+          }
+        }
+        uint32_t o4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // (x0 c - x1 s, x0 s + x1 c) = x1 * (-s, c) + x0 * (c, s)
+          const float2 t = __fmul2_rn(make_float2(p[e].x, p[e].x), cs[e]);
+          const float2 rr = __ffma2_rn(make_float2(p[e].y, p[e].y), ns[e], t);
+          o4[e] = pack_bf16x2(rr.x, rr.y);
+        }
+        st_global(dst + off, make_uint4(o4[0], o4[1], o4[2], o4[3]));
+      }
+    }
   }
+  // error path only (a wait expired): copies issued for later units must land
+  if (lane == 0 && warp + kk * kQkWarps < units)
+    for (int jj = kk + 1; jj < kk + kQkSlots && warp + jj * kQkWarps < units; ++jj)
+      mbar_wait(bar0 + 8u * (uint32_t)(jj % kQkSlots), (uint32_t)((jj / kQkSlots) & 1), fault);
 }
 
 template <int kD, int kMode, bool kPre>
 int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, bool& taken) {
   constexpr int kParts = kMode == kPack ? 3 : 2;
+  constexpr int kHPI = 32 / (kD / 8);
   taken = false;
   const uint32_t unit_bytes = a.heads * kD * 2u;
   const uint32_t slot_bytes = (unit_bytes + 127u) & ~127u;
-  // slot count a multiple of the consumer count: each slot belongs to one
-  // consumer warp, so no warp can wait on a slot more than one phase ahead
-  int slots = (int)((192u * 1024u) / slot_bytes) / kQkConsumers * kQkConsumers;
-  if (slots < kQkConsumers) return JO_OK;  // units too large to stage: caller uses the direct path
-  if (slots > 4 * kQkConsumers) slots = 4 * kQkConsumers;
+  if ((int64_t)a.heads > (int64_t)kQkMaxIt * kHPI) return JO_OK;  // too many heads to hold: direct path
+  const size_t smem = 256 + (size_t)kQkWarps * kQkSlots * slot_bytes;
+  if (smem > 220 * 1024) return JO_OK;
   taken = true;
   auto kern = qk_staged_kernel<kD, kMode, kPre>;
   static bool attr = false;
@@ -305,16 +368,11 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
       return fail(JO_ERR_CUDA, "qk kernel: cannot reserve shared memory");
     attr = true;
   }
-  const size_t smem = (size_t)slots * slot_bytes + ((2 * slots * 8 + 127) & ~127);
   const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * a.heads);
-  int64_t grid = di->sm_count;
-  int64_t per = cdiv(ntok, grid);
-  if (per < 4) {  // small problems: fewer CTAs with a few tokens each
-    per = 4;
-    grid = cdiv(ntok, per);
-  }
-  grid = cdiv(ntok, per);
-  kern<<<(unsigned)grid, kQkThreads, smem, st>>>(a, (int)per, slots, slot_bytes, di->fault);
+  int64_t per = cdiv(ntok, di->sm_count);
+  if (per < 2) per = 2;
+  const int64_t grid = cdiv(ntok, per);
+  kern<<<(unsigned)grid, kQkWarps * 32, smem, st>>>(a, (int)per, slot_bytes, di->fault);
   return after_launch("qk_staged_kernel");
 }
 

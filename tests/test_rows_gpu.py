@@ -119,9 +119,12 @@ def quant_inputs(M, N, dt, seed):
     x = rand((M, N), dt, seed)
     if M > 3:
         x[0].zero_()  # zero row: scale 1e-8/448, q = 0
-        x[1] *= 1e-3
+        x[1] *= 1e-3  # in fp16 some of these underflow to +-0: the byte keeps the sign (0x00 / 0x80)
         x[2] *= 300.0
         x[3, 5] = 448.0 * 3  # a row whose max sits far from the bulk
+    if M > 4 and N > 8:
+        x[4, :4] = torch.tensor([0.0, -0.0, 1.0, -1.0]).to(dt)
+        x[4, 4:8] = -0.0
     return x
 
 
@@ -135,8 +138,11 @@ def test_per_token_quant_bit_exact(jo, dev, dt, shape):
     jo.sgl_per_token_quant_fp8(x.to(dev), q, s)
     rq, rs = ops.per_token_quant_fp8(x)
     assert torch.equal(s.cpu(), rs), "scales differ"
-    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8)), \
-        f"{(q.cpu().view(torch.uint8) != rq.view(torch.uint8)).sum().item()} fp8 bytes differ"
+    qb, rb = q.cpu().view(torch.uint8), rq.view(torch.uint8)
+    if not torch.equal(qb, rb):
+        i = (qb != rb).nonzero()[0].tolist()
+        raise AssertionError(f"{(qb != rb).sum().item()} fp8 bytes differ; first at {i}: x={x[i[0], i[1]].item()!r} "
+                             f"got {qb[i[0], i[1]].item():#04x} want {rb[i[0], i[1]].item():#04x}")
 
 
 def test_per_token_quant_reference_assert(jo, dev):
