@@ -297,6 +297,61 @@ class Gemm(Workload):
         return ((x["aq"].float() * x["sa"]) @ (x["bq"] * x["sb"])).to(BF)
 
 
+class Chain(Workload):
+    """One MMDoubleStreamBlock forward for one streaming chunk:
+    10800 video + 512 text tokens, hidden 3072, 24 x 128 heads, FFN 12288, KV cache of
+    4 prior chunks; random-init weights; video tokens sharded over the ranks (SP)."""
+
+    name = "chain"
+    desc = "per-block op chain, 1 chunk: 10800 img + 512 txt tokens, cache 4 chunks (BASELINE configs[4])"
+    D, H, F, L, T, CACHE = 3072, 24, 12288, 10800, 512, 4 * 10800
+
+    def __init__(self):
+        self.shape = {"hidden": self.D, "heads": self.H, "ffn": self.F, "img_tokens": self.L, "txt_tokens": self.T,
+                      "cache_tokens": self.CACHE, "weights": "random init N(0,0.02), FP8 per-channel"}
+        self.world, self.rank, self.group = 1, 0, None
+
+    def flops(self):
+        D, F, L, T = self.D, self.F, self.L, self.T
+        gemm = 2 * (L + T) * D * (3 * D + D + 2 * F)
+        attn = 4 * (L + T) * (self.CACHE + L + T) * D
+        return gemm + attn
+
+    def algo_bytes(self):
+        return 0
+
+    def make(self, dev, seed):
+        from joyomni_ops import chain, rope
+
+        local = self.L // self.world
+        g = torch.Generator().manual_seed(seed)
+        w = chain.random_block_weights(self.D, self.H, self.F, device=dev, seed=seed)
+        img = torch.randn(local, self.D, generator=g).to(BF).to(dev)
+        txt = torch.randn(self.T, self.D, generator=g).to(BF).to(dev)
+        vec = (0.1 * torch.randn(6, self.D, generator=g)).to(BF).to(dev)
+        cos, sin = rope.video_chunk_tables(3, 45, 80, 7, dims=(44, 42, 42))
+        b0, b1 = chain.shard_range(self.L, self.world, self.rank)
+        cos, sin = cos[b0:b1].to(dev), sin[b0:b1].to(dev)
+        bufs = chain.KVBuffers(self.CACHE, self.L, self.T, self.H, self.D // self.H, self.world, dev)
+        bufs.k.normal_()
+        bufs.v.normal_()
+        side = torch.cuda.Stream()
+        st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side)
+        out = self.step(st)
+        return dict(st, inputs={"img": img, "txt": txt}, outputs={"img_out": out[0], "txt_out": out[1]})
+
+    def step(self, st):
+        return st["chain"].block_forward(st["img"], st["txt"], st["vec"], st["cos"], st["sin"], st["w"], st["bufs"],
+                                         group=self.group, rank=self.rank, side_stream=st["side"])
+
+    def e2e_step(self, st, host_in, host_out):
+        st["img"].copy_(host_in["img"], non_blocking=True)
+        st["txt"].copy_(host_in["txt"], non_blocking=True)
+        a, b = self.step(st)
+        host_out["img_out"].copy_(a, non_blocking=True)
+        host_out["txt_out"].copy_(b, non_blocking=True)
+
+
 def measure_fp8_peak(dev, seconds=1.0):
     """cuBLASLt FP8 (torch._scaled_mm, 8192^3, row/col scales), back to back: TFLOP/s."""
     n = 8192
@@ -334,6 +389,7 @@ def workloads():
         "rmsnorm_quant": RowOp("rmsnorm_quant", 10800, 3072, 2, 1, "RMSNorm->FP8 quant [10800,3072] (configs[3])"),
         "gemm_qkv": Gemm("gemm_qkv", 10800, 9216, 3072, "FP8 GEMM QKV projection [10800,3072]x[3072,9216] (configs[3])"),
         "gemm_up": Gemm("gemm_up", 10800, 12288, 3072, "FP8 GEMM MLP-up [10800,3072]x[3072,12288] (configs[3])"),
+        "chain": Chain(),
     }
 
 
@@ -498,9 +554,18 @@ def run_ours(args, wl: Workload):
     torch.cuda.set_device(dev)
     from joyomni_ops import cabi
 
+    if isinstance(wl, Chain):
+        import torch.distributed as dist
+
+        wl.world, wl.rank = world, rank
+        wl.group = dist.group.WORLD if world > 1 else None
+
     # two buffer sets, alternated every step: the working set (2 x in + out) is
     # several times the 126 MB L2, so no step reads what the previous one left
-    sets = [wl.make(dev, seed=1 + rank * 2 + i) for i in range(2)]
+    # (the block chain's working set is ~2 GB by itself: one set)
+    nsets = 1 if isinstance(wl, Chain) else 2
+    sets = [wl.make(dev, seed=1 + rank * 2 + i) for i in range(nsets)]
+    sets = sets * (2 // nsets)
     torch.cuda.synchronize()
     for i in range(max(args.warmup, 3)):
         wl.step(sets[i % 2])
@@ -568,6 +633,29 @@ def run_ours(args, wl: Workload):
         "gpu_launches": int(launches),
         "clocks": clk,
     }
+    if isinstance(wl, Chain):
+        line.update(metric="µs per DiT-block op chain per chunk", value=round(ms * 1e3, 1), unit="us",
+                    higher_is_better=False, scaling="strong")
+        line["config"]["parallelism"] = (f"sequence parallel over {world} GPUs: video tokens sharded, "
+                                         f"NCCL all-gather of the chunk K/V at the attention boundary")
+        line["config"]["flops_per_step"] = wl.flops()
+        line["achieved_tflops"] = round(wl.flops() / (ms * 1e-3) / 1e12, 1)
+        line["roofline"] = {"bound": "tensor", "achieved": line["achieved_tflops"],
+                            "peak": float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+                            if (REPO / "MEASURED_PEAKS.json").exists() else 1590.0,
+                            "unit": "TFLOP/s", "note": "whole block (GEMMs FP8, attention bf16 library) per GPU "
+                                                      "set vs the measured bf16 dense peak of one GPU x N",
+                            "traffic": None}
+        line["roofline"]["peak"] *= world
+        line["roofline"]["frac"] = round(line["achieved_tflops"] / line["roofline"]["peak"], 4)
+        line["e2e"].update(value=round(e2e_step_ms * 1e3, 1), unit="us")
+        line.pop("pct_of_8TBs")
+        line["cpu_baseline"] = {"value": None, "unit": "us", "cores": os.cpu_count(), "kind": "port",
+                                "sample": "not run: the block is ~10 TFLOP (attention over 54k keys), hours of "
+                                          "host-CPU time; the per-op CPU baselines are in the per-op lines"}
+        print(json.dumps(line), flush=True)
+        _finish(world)
+        return
     if isinstance(wl, Gemm):
         line["metric"] = "FP8 GEMM TFLOP/s"
         line["unit"] = "TFLOP/s"

@@ -162,6 +162,9 @@ JO_API int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, co
  * t*out_stride_t + d]: head-major [heads, tokens, D] is (tokens*D, D),
  * token-major [tokens, heads, D] is (D, heads*D).  k_pre_rope (optional,
  * same layout) receives normalised k before rotation.  head_dim in {64,128,256}.
+ * Text mode (cos == sin == NULL): no rotation, and the q/k RMSNorm rounds twice
+ * as the model's RMSNorm does (bf16(x*rsqrt(mean+eps)), then bf16(. * w);
+ * dit.py:289-296, the text rows of fused_joint_qkv_pack.cu:59-79).
  * Replaces the chain deploy/xvideo/models/dit/dit.py:408-429 ->
  * sgl_fused_ops.py:137-168 (two .contiguous() copies + the paired kernel) and
  * the q/k/v part of fused_joint_qkv_pack. */
@@ -224,6 +227,26 @@ JO_API int jo_norm_scale_shift_quant_fp8(void* out_q, int64_t q_row_stride, floa
                                   const void* beta, const void* scale, const void* shift,
                                   int64_t mod_rows, int64_t mod_row_stride, int64_t rows,
                                   int64_t cols, int norm, int dtype, float eps, void* stream);
+
+/* GELU-tanh -> per-token FP8 quant, one pass: y = dtype(gelu_tanh(x)) is rounded
+ * to dtype in registers, then quantised with the jo_per_token_quant_fp8
+ * semantics.  Replaces the MLP's activation + the down-projection's quant
+ * (deploy/xvideo/models/dit/dit.py:508-513 -> fp8_linear.py:133-140). */
+JO_API int jo_gelu_quant_fp8(void* out_q, int64_t q_row_stride, float* out_s, const void* x,
+                             int64_t x_row_stride, int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* gated residual + Norm + modulate -> per-token FP8 quant, one pass:
+ *   h = dtype(residual + x * gate) (written to out_h),
+ *   (out_q, out_s) = quant(dtype(Norm(h) * (1 + scale) + shift)).
+ * Replaces dit.py:525-535 (fused_add_gate, fused_layernorm_modulate and the
+ * MLP-up projection's quant). */
+JO_API int jo_gated_residual_norm_scale_shift_quant_fp8(
+    void* out_h, int64_t h_row_stride, void* out_q, int64_t q_row_stride, float* out_s,
+    const void* residual, int64_t res_row_stride, const void* x, int64_t x_row_stride,
+    const void* gate, int64_t gate_rows, int64_t gate_row_stride, const void* gamma,
+    const void* beta, const void* scale, const void* shift, int64_t mod_rows,
+    int64_t mod_row_stride, int64_t rows, int64_t cols, int norm, int dtype, float eps,
+    void* stream);
 
 #ifdef __cplusplus
 }

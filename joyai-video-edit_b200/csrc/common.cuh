@@ -169,6 +169,17 @@ __device__ __forceinline__ float quant_clamp(float x, float scale) {
   return fminf(fmaxf(v, -kFp8Max), kFp8Max);
 }
 
+// GELU, tanh approximation: x * sigmoid(2u), u = sqrt(2/pi) * (x + 0.044715 x^3);
+// 0.5 * (1 + tanh(u)) == 1 / (1 + exp(-2u)) exactly.  The exp argument is
+// capped so that 1 + e stays finite (x / inf would lose the sign of -0).
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  constexpr float kTwoSqrt2OverPi = 1.5957691216057308f;  // 2 * sqrt(2/pi)
+  const float x3 = x * x * x;
+  const float z = -kTwoSqrt2OverPi * (x + 0.044715f * x3);
+  const float e = __expf(fminf(z, 80.f));
+  return __fdividef(x, 1.f + e);
+}
+
 // 1/sqrt(v) rounded as torch's CPU rsqrt (IEEE sqrt, then IEEE reciprocal).
 __device__ __forceinline__ float rsqrt_ieee(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
 

@@ -20,16 +20,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
-// GELU-tanh: x * sigmoid(2u), u = sqrt(2/pi) * (x + 0.044715 x^3);
-// 0.5 * (1 + tanh(u)) == 1 / (1 + exp(-2u)) exactly.  The exp argument is
-// capped so that 1 + e stays finite (x / inf would lose the sign of -0).
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-  constexpr float kTwoSqrt2OverPi = 1.5957691216057308f;  // 2 * sqrt(2/pi)
-  const float x3 = x * x * x;
-  const float z = -kTwoSqrt2OverPi * (x + 0.044715f * x3);
-  const float e = __expf(fminf(z, 80.f));
-  return __fdividef(x, 1.f + e);
-}
+// gelu_tanh_f (common.cuh): x * sigmoid(2u), the identical form of
+// 0.5 * x * (1 + tanh(u)).
 
 __device__ __forceinline__ float silu_f(float a) {
   const float e = __expf(fminf(-a, 80.f));

@@ -86,7 +86,7 @@ struct QkArgs {
   float eps;
 };
 
-template <int kD, int kMode, bool kPre>
+template <int kD, int kMode, bool kPre, bool kRope>
 __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) {
   constexpr int kTPH = kD / 8;                  // lanes per head row
   constexpr int kRowsPerPass = kThreads / kTPH;  // head rows per CTA per unrolled slot
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
           src = (part[u] ? a.k : a.q) + (int64_t)r * kD + j * 8;
         }
         v[u] = ld_stream(src);
-        if (part[u] < 2) {
+        if (kRope && part[u] < 2) {
           const int64_t co = (int64_t)tok[u] * (kD / 2) + j * 4;
           cs[u] = __ldg(reinterpret_cast<const uint2*>(a.cos + co));
           sn[u] = __ldg(reinterpret_cast<const uint2*>(a.sin + co));
@@ -146,7 +146,27 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
       const float ss = head_sumsq<kTPH>(f);  // all lanes, before any divergence
       if (i >= a.total_rows) continue;       // whole lane group agrees (same i)
       const uint32_t p = part[u];
-      if (p < 2) {
+      if (p < 2 && !kRope) {
+        // text rows: the model's RMSNorm rounds twice (see the staged kernel)
+        const float r = rsqrt_ieee(__fmul_rn(ss, inv_d) + a.eps);
+        const float* w = p == 0 ? wq : wk;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = round_through<__nv_bfloat16>(f[e] * r) * w[e];
+        int64_t dst_off;
+        if constexpr (kMode == kPack)
+          dst_off = (int64_t)head[u] * a.os_h + (int64_t)tok[u] * a.os_t + j * 8;
+        else
+          dst_off = (int64_t)head[u] * kD + j * 8;
+        if constexpr (kPre) {
+          if (p == 1) st_global(a.k_pre + dst_off, Elt<__nv_bfloat16>::pack(f));
+        }
+        __nv_bfloat16* dst;
+        if constexpr (kMode == kPack)
+          dst = a.out[p];
+        else
+          dst = p ? a.k : a.q;
+        st_global(dst + dst_off, Elt<__nv_bfloat16>::pack(f));
+      } else if (p < 2) {
         head_scale(f, p == 0 ? wq : wk, ss, inv_d, a.eps);
         int64_t dst_off;
         if constexpr (kMode == kPack)
@@ -191,7 +211,7 @@ __device__ __forceinline__ float2 bf2f(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
-template <int kD, int kMode, bool kPre>
+template <int kD, int kMode, bool kPre, bool kRope>
 __global__ void __launch_bounds__(kQkWarps * 32, 1)
     qk_staged_kernel(const QkArgs a, int tok_per_cta, uint32_t slot_bytes, unsigned int* fault) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -252,7 +272,7 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
     int part;
     __nv_bfloat16* unit_dst = unit_ptr(i, tok, part);  // kInPlace destination
     float2 cs[4], ns[4];  // (c, s) and (-s, c) per rotated pair
-    if (part < 2) {
+    if (kRope && part < 2) {
       const int64_t rt = kMode == kPack ? tok : tok % a.seq_len;
       const uint2 c2 = __ldg(reinterpret_cast<const uint2*>(a.cos + rt * (kD / 2) + j * 4));
       const uint2 s2 = __ldg(reinterpret_cast<const uint2*>(a.sin + rt * (kD / 2) + j * 4));
@@ -323,6 +343,24 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
         for (int e = 0; e < 4; ++e) p[e] = bf2f(u[e]);
         const float r = rsqrtf(fmaf(ss[q], inv_d, a.eps));
         const float2 r2 = make_float2(r, r);
+        if constexpr (!kRope) {
+          // text rows: the model's RMSNorm rounds twice, bf16(x * r) then bf16(. * w)
+          uint32_t o4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 nrm = bf2f(pack_bf16x2(__fmul_rn(p[e].x, r), __fmul_rn(p[e].y, r)));
+            const float2 y = __fmul2_rn(nrm, w[e]);
+            o4[e] = pack_bf16x2(y.x, y.y);
+          }
+          if constexpr (kPre) {
+            if (part == 1) {
+              const int64_t pre = kMode == kPack ? off : tok * (int64_t)H * kD + off;
+              st_global(a.k_pre + pre, make_uint4(o4[0], o4[1], o4[2], o4[3]));
+            }
+          }
+          st_global(dst + off, make_uint4(o4[0], o4[1], o4[2], o4[3]));
+          continue;
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) p[e] = __fmul2_rn(__fmul2_rn(p[e], r2), w[e]);  // (x * r) * w
         if constexpr (kPre) {
@@ -350,7 +388,7 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
       mbar_wait(bar0 + 8u * (uint32_t)(jj % kQkSlots), (uint32_t)((jj / kQkSlots) & 1), fault);
 }
 
-template <int kD, int kMode, bool kPre>
+template <int kD, int kMode, bool kPre, bool kRope>
 int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, bool& taken) {
   constexpr int kParts = kMode == kPack ? 3 : 2;
   constexpr int kHPI = 32 / (kD / 8);
@@ -361,7 +399,7 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
   const size_t smem = 256 + (size_t)kQkWarps * kQkSlots * slot_bytes;
   if (smem > 220 * 1024) return JO_OK;
   taken = true;
-  auto kern = qk_staged_kernel<kD, kMode, kPre>;
+  auto kern = qk_staged_kernel<kD, kMode, kPre, kRope>;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
@@ -376,9 +414,9 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
   return after_launch("qk_staged_kernel");
 }
 
-template <int kD, int kMode, bool kPre>
+template <int kD, int kMode, bool kPre, bool kRope>
 int launch_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
-  auto kern = qk_norm_rope_kernel<kD, kMode, kPre>;
+  auto kern = qk_norm_rope_kernel<kD, kMode, kPre, kRope>;
   constexpr int chunk = (kThreads / (kD / 8)) * kUnroll;
   const int64_t need = cdiv(a.total_rows, chunk);
   static int occ = 0;  // resident CTAs per SM; identical on every B200
@@ -390,21 +428,28 @@ int launch_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
   return after_launch("qk_norm_rope_kernel");
 }
 
-template <int kD, int kMode, bool kPre>
+template <int kD, int kMode, bool kPre, bool kRope>
 int run_qk(const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
   bool taken = false;
-  const int s = launch_qk_staged<kD, kMode, kPre>(a, st, di, taken);
+  const int s = launch_qk_staged<kD, kMode, kPre, kRope>(a, st, di, taken);
   if (taken) return s;
-  return launch_qk<kD, kMode, kPre>(a, st, di);
+  return launch_qk<kD, kMode, kPre, kRope>(a, st, di);
+}
+
+template <int kD, int kMode>
+int run_qk_flags(bool pre, bool rope, const QkArgs& a, cudaStream_t st, const DeviceInfo* di) {
+  if (rope) return pre ? run_qk<kD, kMode, true, true>(a, st, di) : run_qk<kD, kMode, false, true>(a, st, di);
+  return pre ? run_qk<kD, kMode, true, false>(a, st, di) : run_qk<kD, kMode, false, false>(a, st, di);
 }
 
 template <int kMode>
 int dispatch_qk(int64_t head_dim, bool pre, const QkArgs& a, cudaStream_t st,
                 const DeviceInfo* di) {
+  const bool rope = a.cos != nullptr;
   switch (head_dim) {
-    case 64: return pre ? run_qk<64, kMode, true>(a, st, di) : run_qk<64, kMode, false>(a, st, di);
-    case 128: return pre ? run_qk<128, kMode, true>(a, st, di) : run_qk<128, kMode, false>(a, st, di);
-    case 256: return pre ? run_qk<256, kMode, true>(a, st, di) : run_qk<256, kMode, false>(a, st, di);
+    case 64: return run_qk_flags<64, kMode>(pre, rope, a, st, di);
+    case 128: return run_qk_flags<128, kMode>(pre, rope, a, st, di);
+    case 256: return run_qk_flags<256, kMode>(pre, rope, a, st, di);
     default: return fail(JO_ERR_SHAPE, "head_dim must be 64, 128 or 256, got %lld", (long long)head_dim);
   }
 }
@@ -615,8 +660,10 @@ int jo_qkv_norm_rope_pack(void* out_q, void* out_k, void* out_v, void* k_pre_rop
   if (tokens == 0) return JO_OK;
   if (tokens * 3 * heads > (int64_t)INT32_MAX)
     return fail(JO_ERR_SHAPE, "%s: tokens*3*heads exceeds 2^31", op);
-  if (!out_q || !out_k || !out_v || !qkv || !q_weight || !k_weight || !cos || !sin)
+  if (!out_q || !out_k || !out_v || !qkv || !q_weight || !k_weight)
     return fail(JO_ERR_INVALID, "%s: null operand", op);
+  if ((cos == nullptr) != (sin == nullptr))
+    return fail(JO_ERR_INVALID, "%s: cos and sin must both be given (RoPE) or both be null (text rows)", op);
   if (qkv_row_stride < 3 * heads * head_dim) return fail(JO_ERR_SHAPE, "%s: qkv row stride too small", op);
   const void* ptrs[] = {out_q, out_k, out_v, qkv, q_weight, k_weight};
   for (const void* p : ptrs)

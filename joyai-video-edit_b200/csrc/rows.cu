@@ -230,4 +230,57 @@ int jo_gated_residual_norm_scale_shift(
                       : launch_rows<kRms, kResidGate, kStoreY>(dtype, a, st, true);
 }
 
+int jo_gelu_quant_fp8(void* out_q, int64_t q_row_stride, float* out_s, const void* x, int64_t x_row_stride,
+                      int64_t rows, int64_t cols, int dtype, void* stream) {
+  RowArgs a{};
+  a.out_q = (uint8_t*)out_q;
+  a.q_stride = q_row_stride;
+  a.out_s = out_s;
+  a.x = x;
+  a.x_stride = x_row_stride;
+  a.rows = rows;
+  a.cols = cols;
+  if (int s = check_common(a, "gelu_quant_fp8")) return s;
+  if (rows > 0 && (!out_q || !out_s)) return fail(JO_ERR_INVALID, "gelu_quant_fp8: outputs must be non-null");
+  return launch_rows<kNoNorm, kGeluX, kQuantY>(dtype, a, (cudaStream_t)stream, false);
+}
+
+int jo_gated_residual_norm_scale_shift_quant_fp8(
+    void* out_h, int64_t h_row_stride, void* out_q, int64_t q_row_stride, float* out_s, const void* residual,
+    int64_t res_row_stride, const void* x, int64_t x_row_stride, const void* gate, int64_t gate_rows,
+    int64_t gate_row_stride, const void* gamma, const void* beta, const void* scale, const void* shift,
+    int64_t mod_rows, int64_t mod_row_stride, int64_t rows, int64_t cols, int norm, int dtype, float eps,
+    void* stream) {
+  RowArgs a{};
+  a.out_h = out_h;
+  a.h_stride = h_row_stride;
+  a.out_q = (uint8_t*)out_q;
+  a.q_stride = q_row_stride;
+  a.out_s = out_s;
+  a.x = x;
+  a.x_stride = x_row_stride;
+  a.res = residual;
+  a.res_stride = res_row_stride;
+  a.gate = gate;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.rows = rows;
+  a.cols = cols;
+  a.eps = eps;
+  const char* op = "gated_residual_norm_scale_shift_quant_fp8";
+  if (int s = check_common(a, op)) return s;
+  if (rows > 0 && cols > 0 && (!out_h || !out_q || !out_s || !residual || !gate))
+    return fail(JO_ERR_INVALID, "%s: null operand", op);
+  if (gate_rows != 1 && gate_rows != rows)
+    return fail(JO_ERR_SHAPE, "%s: gate rows must be 1 or %lld", op, (long long)rows);
+  a.gate_stride = gate_rows == 1 ? 0 : gate_row_stride;
+  if (int s = mod_setup(a, scale, shift, mod_rows, mod_row_stride, rows, op)) return s;
+  const int nk = norm_code(norm, op);
+  if (nk < 0) return nk;
+  if (nk == kRms) a.beta = nullptr;
+  cudaStream_t st = (cudaStream_t)stream;
+  return nk == kLayer ? launch_rows<kLayer, kResidGate, kQuantY>(dtype, a, st, false)
+                      : launch_rows<kRms, kResidGate, kQuantY>(dtype, a, st, false);
+}
+
 }  // extern "C"

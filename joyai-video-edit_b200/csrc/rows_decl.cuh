@@ -7,7 +7,7 @@ namespace jo {
 namespace rows {
 
 enum NormKind { kNoNorm = 0, kLayer = 1, kRms = 2 };
-enum ProKind { kLoadX = 0, kResidGate = 1 };
+enum ProKind { kLoadX = 0, kResidGate = 1, kGeluX = 2 };  // kGeluX: x -> T(gelu_tanh(x))
 enum EpiKind { kStoreY = 0, kQuantY = 1, kNoY = 2 };
 
 struct RowArgs {

@@ -11,5 +11,8 @@ template int launch_rows_t<__half, kNoNorm, kLoadX, kQuantY>(const RowArgs&, cud
 template int launch_rows_t<__half, kRms, kLoadX, kQuantY>(const RowArgs&, cudaStream_t);
 template int launch_rows_t<__half, kLayer, kLoadX, kQuantY>(const RowArgs&, cudaStream_t);
 template int launch_rows_t<__half, kNoNorm, kResidGate, kNoY>(const RowArgs&, cudaStream_t);
+template int launch_rows_t<__half, kNoNorm, kGeluX, kQuantY>(const RowArgs&, cudaStream_t);
+template int launch_rows_t<__half, kLayer, kResidGate, kQuantY>(const RowArgs&, cudaStream_t);
+template int launch_rows_t<__half, kRms, kResidGate, kQuantY>(const RowArgs&, cudaStream_t);
 }  // namespace rows
 }  // namespace jo

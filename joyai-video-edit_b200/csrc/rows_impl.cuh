@@ -97,6 +97,16 @@ __device__ __forceinline__ uint4 resid_vec(const RowArgs& a, int64_t row, int id
   return h;
 }
 
+// GELU-tanh of one vector, rounded to T (the tensor the unfused chain materialises).
+template <typename T>
+__device__ __forceinline__ uint4 gelu_vec(const uint4& u) {
+  float f[Elt<T>::kVec];
+  Elt<T>::unpack(u, f);
+#pragma unroll
+  for (int e = 0; e < Elt<T>::kVec; ++e) f[e] = gelu_tanh_f(f[e]);
+  return Elt<T>::pack(f);
+}
+
 // kHDone: the caller already formed h (kResidGate) into raw and stored it.
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp, bool kHDone = false>
 __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT],
@@ -441,7 +451,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     if (i >= units) return;
     const int64_t row = r0 + i;
     const uint32_t bar = bar0 + 8u * (uint32_t)(k % m), dst = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
-    if constexpr (kPro == kLoadX) {
+    if constexpr (kPro != kResidGate) {
       mbar_expect_tx(bar, row_bytes);
       bulk_load(dst, reinterpret_cast<const T*>(a.x) + row * a.x_stride, row_bytes, bar);
     } else {
@@ -464,6 +474,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       if (idx < nvec) {
         if constexpr (kPro == kLoadX)
           raw[v] = lds128(sl + idx * 16);
+        else if constexpr (kPro == kGeluX)
+          raw[v] = gelu_vec<T>(lds128(sl + idx * 16));
         else  // h = residual + x * gate straight from the slot
           raw[v] = resid_vec<T>(a, row, idx, lds128(sl + idx * 16), lds128(sl + row_bytes + idx * 16));
       }
@@ -503,11 +515,18 @@ __global__ void __launch_bounds__(kVPT <= 4 ? 1024 : (kVPT <= 8 ? 512 : 256))
     if (idx < nvec) {
       if constexpr (kPro == kLoadX) {
         raw[i] = ld_stream(xr + (int64_t)idx * V);
+      } else if constexpr (kPro == kGeluX) {
+        raw[i] = ld_stream(xr + (int64_t)idx * V);
       } else {
         xv[i] = ld_stream(xr + (int64_t)idx * V);
         raw[i] = ld_stream(rr + (int64_t)idx * V);
       }
     }
+  }
+  if constexpr (kPro == kGeluX) {
+#pragma unroll
+    for (int i = 0; i < kVPT; ++i)
+      if (g + i * G < nvec) raw[i] = gelu_vec<T>(raw[i]);
   }
   row_math<T, kVPT, kNorm, kPro, kEpi, false>(a, row, raw, xv, g, G, smem);
 }
@@ -536,21 +555,26 @@ __global__ void __launch_bounds__(256) row_scalar_kernel(const RowArgs a) {
     src = hr;  // each thread re-reads only the elements it wrote itself
   }
   if constexpr (kEpi == kNoY) return;
+  auto xval = [&](int c) {
+    const float v = Elt<T>::to_f(src[c]);
+    if constexpr (kPro == kGeluX) return round_through<T>(gelu_tanh_f(v));
+    return v;
+  };
   float mean = 0.f, rstd = 1.f;
   if constexpr (kNorm == kLayer) {
     float s = 0.f;
-    for (int c = g; c < n; c += G) s += Elt<T>::to_f(src[c]);
+    for (int c = g; c < n; c += G) s += xval(c);
     mean = __fdiv_rn(row_reduce_sum<false>(s, smem), (float)n);
     float q = 0.f;
     for (int c = g; c < n; c += G) {
-      const float d = Elt<T>::to_f(src[c]) - mean;
+      const float d = xval(c) - mean;
       q += d * d;
     }
     rstd = rsqrt_ieee(__fdiv_rn(row_reduce_sum<false>(q, smem), (float)n) + a.eps);
   } else if constexpr (kNorm == kRms) {
     float q = 0.f;
     for (int c = g; c < n; c += G) {
-      const float v = Elt<T>::to_f(src[c]);
+      const float v = xval(c);
       q += v * v;
     }
     rstd = rsqrt_ieee(__fdiv_rn(row_reduce_sum<false>(q, smem), (float)n) + a.eps);
@@ -559,7 +583,7 @@ __global__ void __launch_bounds__(256) row_scalar_kernel(const RowArgs a) {
   const T* scr = has_mod ? reinterpret_cast<const T*>(a.scale) + row * a.mod_stride : nullptr;
   const T* shr = has_mod ? reinterpret_cast<const T*>(a.shift) + row * a.mod_stride : nullptr;
   auto y_at = [&](int c) {
-    return norm_elem<kNorm>(Elt<T>::to_f(src[c]), mean, rstd, has_g ? ldf<T>(a.gamma, c) : 1.f,
+    return norm_elem<kNorm>(xval(c), mean, rstd, has_g ? ldf<T>(a.gamma, c) : 1.f,
                             has_b ? ldf<T>(a.beta, c) : 0.f, has_mod ? Elt<T>::to_f(scr[c]) : 0.f,
                             has_mod ? Elt<T>::to_f(shr[c]) : 0.f, has_g, has_b, has_mod);
   };

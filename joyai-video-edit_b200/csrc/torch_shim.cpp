@@ -327,43 +327,6 @@ torch::Tensor fp8_scaled_mm(const torch::Tensor& mat_a, const torch::Tensor& mat
 
 // ------------------------------------------------------------------ new fused ops
 
-std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> qkv_norm_rope_pack(
-    const torch::Tensor& qkv, int64_t num_heads, const torch::Tensor& q_weight, const torch::Tensor& k_weight,
-    const torch::Tensor& cos, const torch::Tensor& sin, double eps, bool head_major,
-    const c10::optional<torch::Tensor>& k_pre_rope) {
-  JO_CHECK_CUDA(qkv);
-  TORCH_CHECK(qkv.dim() == 2, "qkv must be 2D [tokens, 3*heads*head_dim]");
-  TORCH_CHECK(qkv.stride(1) == 1, "qkv last dim must be contiguous");
-  JO_CHECK_DTYPE(qkv, torch::kBFloat16);
-  TORCH_CHECK(num_heads > 0 && qkv.size(1) % (3 * num_heads) == 0, "qkv width must be 3*num_heads*head_dim");
-  const int64_t L = qkv.size(0), D = qkv.size(1) / (3 * num_heads);
-  TORCH_CHECK(D == 64 || D == 128 || D == 256, "head_dim must be 64, 128 or 256, got ", D);
-  JO_CHECK_INPUT(q_weight, torch::kBFloat16);
-  JO_CHECK_INPUT(k_weight, torch::kBFloat16);
-  JO_CHECK_INPUT(cos, torch::kBFloat16);
-  JO_CHECK_INPUT(sin, torch::kBFloat16);
-  TORCH_CHECK(q_weight.numel() == D && k_weight.numel() == D, "weight size must match head_dim");
-  TORCH_CHECK(cos.dim() == 2 && cos.size(0) == L && cos.size(1) == D / 2, "cos shape must be [tokens, head_dim/2]");
-  TORCH_CHECK(sin.sizes() == cos.sizes(), "sin shape must match cos");
-  const c10::cuda::CUDAGuard guard(qkv.device());
-  auto shape = head_major ? std::vector<int64_t>{num_heads, L, D} : std::vector<int64_t>{L, num_heads, D};
-  auto q = torch::empty(shape, qkv.options());
-  auto k = torch::empty(shape, qkv.options());
-  auto v = torch::empty(shape, qkv.options());
-  void* pre = nullptr;
-  if (k_pre_rope.has_value() && k_pre_rope->defined()) {
-    JO_CHECK_INPUT(*k_pre_rope, torch::kBFloat16);
-    TORCH_CHECK(k_pre_rope->sizes() == k.sizes(), "k_pre_rope must have the output shape ", k.sizes());
-    pre = k_pre_rope->data_ptr();
-  }
-  const int64_t sh = head_major ? L * D : D, st = head_major ? D : num_heads * D;
-  jo_check(jo_qkv_norm_rope_pack(q.data_ptr(), k.data_ptr(), v.data_ptr(), pre, sh, st, qkv.data_ptr(), qkv.stride(0),
-                                 L, num_heads, D, q_weight.data_ptr(), k_weight.data_ptr(), cos.data_ptr(),
-                                 sin.data_ptr(), (float)eps, stream_of(qkv)),
-           "qkv_norm_rope_pack");
-  return std::make_tuple(q, k, v);
-}
-
 torch::Tensor as_rows(const torch::Tensor& t, int64_t cols, const char* name) {
   TORCH_CHECK(t.size(-1) == cols, name, " last dim must be ", cols);
   TORCH_CHECK(t.stride(-1) == 1, name, " last dim must be contiguous");
@@ -378,6 +341,121 @@ std::pair<int64_t, int64_t> gate_rows(const torch::Tensor& gate, int64_t M, int6
   if (gr == 1) return {1, 0};
   TORCH_CHECK(gate.dim() == 2, "a per-row gate must be 2D [M, N]");
   return {gr, gate.stride(0)};
+}
+
+// Shared checks of the qkv pack ops; returns (tokens, head_dim).
+std::pair<int64_t, int64_t> check_qkv_pack(const torch::Tensor& qkv, int64_t num_heads, const torch::Tensor& q_weight,
+                                           const torch::Tensor& k_weight, const c10::optional<torch::Tensor>& cos,
+                                           const c10::optional<torch::Tensor>& sin) {
+  JO_CHECK_CUDA(qkv);
+  TORCH_CHECK(qkv.dim() == 2, "qkv must be 2D [tokens, 3*heads*head_dim]");
+  TORCH_CHECK(qkv.stride(1) == 1, "qkv last dim must be contiguous");
+  JO_CHECK_DTYPE(qkv, torch::kBFloat16);
+  TORCH_CHECK(num_heads > 0 && qkv.size(1) % (3 * num_heads) == 0, "qkv width must be 3*num_heads*head_dim");
+  const int64_t L = qkv.size(0), D = qkv.size(1) / (3 * num_heads);
+  TORCH_CHECK(D == 64 || D == 128 || D == 256, "head_dim must be 64, 128 or 256, got ", D);
+  JO_CHECK_INPUT(q_weight, torch::kBFloat16);
+  JO_CHECK_INPUT(k_weight, torch::kBFloat16);
+  TORCH_CHECK(q_weight.numel() == D && k_weight.numel() == D, "weight size must match head_dim");
+  const bool hc = cos.has_value() && cos->defined(), hs = sin.has_value() && sin->defined();
+  TORCH_CHECK(hc == hs, "cos and sin must both be given (RoPE) or both be None (text rows, no rotation)");
+  if (hc) {
+    JO_CHECK_INPUT(*cos, torch::kBFloat16);
+    JO_CHECK_INPUT(*sin, torch::kBFloat16);
+    TORCH_CHECK(cos->dim() == 2 && cos->size(0) == L && cos->size(1) == D / 2,
+                "cos shape must be [tokens, head_dim/2]");
+    TORCH_CHECK(sin->sizes() == cos->sizes(), "sin shape must match cos");
+  }
+  return {L, D};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> qkv_norm_rope_pack(
+    const torch::Tensor& qkv, int64_t num_heads, const torch::Tensor& q_weight, const torch::Tensor& k_weight,
+    const c10::optional<torch::Tensor>& cos, const c10::optional<torch::Tensor>& sin, double eps, bool head_major,
+    const c10::optional<torch::Tensor>& k_pre_rope) {
+  const auto [L, D] = check_qkv_pack(qkv, num_heads, q_weight, k_weight, cos, sin);
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto shape = head_major ? std::vector<int64_t>{num_heads, L, D} : std::vector<int64_t>{L, num_heads, D};
+  auto q = torch::empty(shape, qkv.options());
+  auto k = torch::empty(shape, qkv.options());
+  auto v = torch::empty(shape, qkv.options());
+  void* pre = nullptr;
+  if (k_pre_rope.has_value() && k_pre_rope->defined()) {
+    JO_CHECK_INPUT(*k_pre_rope, torch::kBFloat16);
+    TORCH_CHECK(k_pre_rope->sizes() == k.sizes(), "k_pre_rope must have the output shape ", k.sizes());
+    pre = k_pre_rope->data_ptr();
+  }
+  const int64_t sh = head_major ? L * D : D, st = head_major ? D : num_heads * D;
+  jo_check(jo_qkv_norm_rope_pack(q.data_ptr(), k.data_ptr(), v.data_ptr(), pre, sh, st, qkv.data_ptr(), qkv.stride(0),
+                                 L, num_heads, D, q_weight.data_ptr(), k_weight.data_ptr(), opt_ptr(cos),
+                                 opt_ptr(sin), (float)eps, stream_of(qkv)),
+           "qkv_norm_rope_pack");
+  return std::make_tuple(q, k, v);
+}
+
+// Same op writing into caller-provided [tokens, heads, head_dim] views (any
+// token/head strides, shared by q/k/v): e.g. slices of persistent Q and KV
+// buffers, so no concatenation copy is needed before attention.
+void qkv_norm_rope_pack_into(const torch::Tensor& qkv, int64_t num_heads, const torch::Tensor& q_weight,
+                             const torch::Tensor& k_weight, const c10::optional<torch::Tensor>& cos,
+                             const c10::optional<torch::Tensor>& sin, double eps, torch::Tensor& q_out,
+                             torch::Tensor& k_out, torch::Tensor& v_out) {
+  const auto [L, D] = check_qkv_pack(qkv, num_heads, q_weight, k_weight, cos, sin);
+  for (const torch::Tensor* t : {&q_out, &k_out, &v_out}) {
+    JO_CHECK_CUDA(*t);
+    JO_CHECK_DTYPE(*t, torch::kBFloat16);
+    TORCH_CHECK(t->dim() == 3 && t->size(0) == L && t->size(1) == num_heads && t->size(2) == D,
+                "outputs must be [tokens, heads, head_dim] views, got ", t->sizes());
+    TORCH_CHECK(t->stride(2) == 1 && t->stride(0) == q_out.stride(0) && t->stride(1) == q_out.stride(1),
+                "q/k/v outputs must share token and head strides with a contiguous last dim");
+  }
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  jo_check(jo_qkv_norm_rope_pack(q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), nullptr, q_out.stride(1),
+                                 q_out.stride(0), qkv.data_ptr(), qkv.stride(0), L, num_heads, D, q_weight.data_ptr(),
+                                 k_weight.data_ptr(), opt_ptr(cos), opt_ptr(sin), (float)eps, stream_of(qkv)),
+           "qkv_norm_rope_pack_into");
+}
+
+std::tuple<torch::Tensor, torch::Tensor> gelu_quant_fp8(const torch::Tensor& x) {
+  JO_CHECK_CUDA(x);
+  TORCH_CHECK(x.dim() == 2 && x.stride(-1) == 1, "x must be 2D [M, N] with contiguous rows");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto q = torch::empty({x.size(0), x.size(1)}, x.options().dtype(torch::kFloat8_e4m3fn));
+  auto s = torch::empty({x.size(0), 1}, x.options().dtype(torch::kFloat32));
+  jo_check(jo_gelu_quant_fp8(q.data_ptr(), x.size(1), s.data_ptr<float>(), x.data_ptr(), x.stride(0), x.size(0),
+                             x.size(1), dt_code(x.scalar_type()), stream_of(x)),
+           "gelu_quant_fp8");
+  return std::make_tuple(q, s);
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> gated_residual_norm_scale_shift_quant_fp8(
+    const torch::Tensor& residual, const torch::Tensor& x, const torch::Tensor& gate,
+    const c10::optional<torch::Tensor>& gamma, const c10::optional<torch::Tensor>& beta, const torch::Tensor& scale,
+    const torch::Tensor& shift, int64_t norm_type, double eps) {
+  JO_CHECK_CUDA(residual);
+  JO_CHECK_CUDA(x);
+  TORCH_CHECK(residual.sizes() == x.sizes(), "residual and x must have the same shape");
+  TORCH_CHECK(residual.dtype() == x.dtype() && x.dtype() == gate.dtype(), "dtypes must match");
+  TORCH_CHECK(norm_type == 0 || norm_type == 1, "norm_type must be 0 (layer) or 1 (rms)");
+  const int64_t N = x.size(-1);
+  auto r2 = as_rows(residual.contiguous(), N, "residual");
+  auto x2 = as_rows(x.contiguous(), N, "x");
+  auto g = gate_rows(gate, x2.size(0), N);
+  auto sc = scale.reshape({-1, N});
+  auto sh = shift.reshape({-1, N});
+  check_mod(x2, sc, sh);
+  check_affine(x2, gamma, beta);
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto h = torch::empty_like(r2);
+  auto q = torch::empty({x2.size(0), N}, x.options().dtype(torch::kFloat8_e4m3fn));
+  auto s = torch::empty({x2.size(0), 1}, x.options().dtype(torch::kFloat32));
+  jo_check(jo_gated_residual_norm_scale_shift_quant_fp8(
+               h.data_ptr(), N, q.data_ptr(), N, s.data_ptr<float>(), r2.data_ptr(), N, x2.data_ptr(), N,
+               gate.data_ptr(), g.first, g.second, opt_ptr(gamma), opt_ptr(beta), sc.data_ptr(), sh.data_ptr(),
+               sc.size(0), sc.stride(0), x2.size(0), N, (int)norm_type, dt_code(x.scalar_type()), (float)eps,
+               stream_of(x)),
+           "gated_residual_norm_scale_shift_quant_fp8");
+  return std::make_tuple(h.view(residual.sizes()), q, s);
 }
 
 torch::Tensor gated_residual(const torch::Tensor& residual, const torch::Tensor& x, const torch::Tensor& gate) {
@@ -525,8 +603,15 @@ TORCH_LIBRARY(joyomni_ops, m) {
       "ScalarType out_dtype, Tensor? bias) -> Tensor");
   // New fused ops on the same path.
   m.def(
-      "qkv_norm_rope_pack(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor cos, "
-      "Tensor sin, float eps, bool head_major, Tensor(a!)? k_pre_rope) -> (Tensor, Tensor, Tensor)");
+      "qkv_norm_rope_pack(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
+      "Tensor? sin, float eps, bool head_major, Tensor(a!)? k_pre_rope) -> (Tensor, Tensor, Tensor)");
+  m.def(
+      "qkv_norm_rope_pack_into(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
+      "Tensor? sin, float eps, Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out) -> ()");
+  m.def("gelu_quant_fp8(Tensor x) -> (Tensor, Tensor)");
+  m.def(
+      "gated_residual_norm_scale_shift_quant_fp8(Tensor residual, Tensor x, Tensor gate, Tensor? gamma, "
+      "Tensor? beta, Tensor scale, Tensor shift, int norm_type, float eps) -> (Tensor, Tensor, Tensor)");
   m.def("gated_residual(Tensor residual, Tensor x, Tensor gate) -> Tensor");
   m.def(
       "gated_residual_norm_scale_shift(Tensor residual, Tensor x, Tensor gate, Tensor? gamma, "
@@ -551,6 +636,9 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("sgl_per_token_quant_fp8", &sgl_per_token_quant_fp8);
   m.impl("fp8_scaled_mm", &fp8_scaled_mm);
   m.impl("qkv_norm_rope_pack", &qkv_norm_rope_pack);
+  m.impl("qkv_norm_rope_pack_into", &qkv_norm_rope_pack_into);
+  m.impl("gelu_quant_fp8", &gelu_quant_fp8);
+  m.impl("gated_residual_norm_scale_shift_quant_fp8", &gated_residual_norm_scale_shift_quant_fp8);
   m.impl("gated_residual", &gated_residual);
   m.impl("gated_residual_norm_scale_shift", &gated_residual_norm_scale_shift);
   m.impl("gelu_tanh", &gelu_tanh);

@@ -46,6 +46,9 @@ __all__ = [
     "timestep_embedding",
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
+    "qkv_norm_rope_pack_into",
+    "gelu_quant_fp8",
+    "gated_residual_norm_scale_shift_quant_fp8",
     "library_path",
 ]
 
@@ -111,6 +114,25 @@ def _fake_qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, 
     D = qkv.shape[1] // (3 * num_heads)
     shape = (num_heads, L, D) if head_major else (L, num_heads, D)
     return qkv.new_empty(shape), qkv.new_empty(shape), qkv.new_empty(shape)
+
+
+@torch.library.register_fake("joyomni_ops::qkv_norm_rope_pack_into")
+def _fake_qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out):
+    return None
+
+
+@torch.library.register_fake("joyomni_ops::gelu_quant_fp8")
+def _fake_gelu_quant_fp8(x):
+    return (x.new_empty(x.shape, dtype=torch.float8_e4m3fn),
+            x.new_empty((x.shape[0], 1), dtype=torch.float32))
+
+
+@torch.library.register_fake("joyomni_ops::gated_residual_norm_scale_shift_quant_fp8")
+def _fake_gated_residual_norm_scale_shift_quant_fp8(residual, x, gate, gamma, beta, scale, shift, norm_type, eps):
+    n = residual.shape[-1]
+    m = residual.numel() // n
+    return (residual.new_empty(residual.shape), residual.new_empty((m, n), dtype=torch.float8_e4m3fn),
+            residual.new_empty((m, 1), dtype=torch.float32))
 
 
 @torch.library.register_fake("joyomni_ops::gated_residual")
@@ -204,10 +226,28 @@ def qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps=1e-6, h
                        k_pre_rope: Optional[torch.Tensor] = None):
     """qkv [L, 3*H*D] (K H D order) -> q, k, v with per-head RMSNorm + RoPE on q/k.
 
-    Outputs are [H, L, D] (head_major=True) or [L, H, D].  cos/sin: bf16 [L, D/2].
+    Outputs are [H, L, D] (head_major=True) or [L, H, D].  cos/sin: bf16 [L, D/2],
+    or both None for text rows (no rotation; the model RMSNorm's double rounding).
     k_pre_rope, if given, receives the normalised k before rotation (same layout).
     """
     return _ops.qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, head_major, k_pre_rope)
+
+
+def qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, q_out, k_out, v_out, eps=1e-6):
+    """qkv_norm_rope_pack writing into [L, H, D] views (e.g. slices of persistent Q / KV buffers)."""
+    _ops.qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out)
+
+
+def gelu_quant_fp8(x):
+    """(q e4m3 [M, N], scale fp32 [M, 1]) of bf16(gelu_tanh(x))."""
+    return _ops.gelu_quant_fp8(x)
+
+
+def gated_residual_norm_scale_shift_quant_fp8(residual, x, gate, scale, shift, norm_type="layer", eps=1e-6,
+                                              gamma=None, beta=None):
+    """(h, q, s): h = residual + x*gate; (q, s) = FP8 quant of Norm(h)*(1+scale)+shift."""
+    return _ops.gated_residual_norm_scale_shift_quant_fp8(residual, x, gate, gamma, beta, scale, shift,
+                                                          _norm_code(norm_type), eps)
 
 
 def gated_residual(residual, x, gate):

@@ -59,6 +59,9 @@ SIGNATURES = {
     "jo_timestep_embedding": [P, P, I64, I64, I32, F32, F32, F32, P],
     "jo_rmsnorm_quant_fp8": [P, I64, P, P, I64, P, I64, I64, I32, F32, P],
     "jo_norm_scale_shift_quant_fp8": [P, I64, P, P, I64, P, P, P, P, I64, I64, I64, I64, I32, I32, F32, P],
+    "jo_gelu_quant_fp8": [P, I64, P, P, I64, I64, I64, I32, P],
+    "jo_gated_residual_norm_scale_shift_quant_fp8": [P, I64, P, I64, P, P, I64, P, I64, P, I64, I64, P, P, P, P,
+                                                     I64, I64, I64, I64, I32, I32, F32, P],
 }
 _RESTYPES = {"jo_status_name": C.c_char_p, "jo_last_error": C.c_char_p, "jo_launch_count": C.c_uint64}
 

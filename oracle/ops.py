@@ -284,6 +284,71 @@ def fp8_scaled_mm(a_q, b_q, scale_a, scale_b, bias: Optional[torch.Tensor], out_
     return d.to(out_dtype)
 
 
+def qkv_text_pack(qkv, num_heads, qw, kw, eps):
+    """Text rows of the joint pack: q/k RMSNorm with the model's double rounding
+    (joyomni_ops/tests/test_parity_light.py:160-165), no RoPE; v copied.
+    qkv [L, 3*H*D] -> token-major q, k, v [L, H, D]."""
+    L = qkv.shape[0]
+    D = qkv.shape[1] // (3 * num_heads)
+    x = qkv.view(L, 3, num_heads, D)
+
+    def norm(t, w):
+        tf = t.float()
+        n = (tf * torch.rsqrt(tf.square().mean(-1, keepdim=True) + eps)).to(torch.bfloat16)
+        return n * w
+
+    return norm(x[:, 0], qw), norm(x[:, 1], kw), x[:, 2].clone()
+
+
+def attention(q, k, v):
+    """Non-causal softmax attention in fp32 on token-major [S, H, D] tensors -> dtype [Sq, H*D]
+    (the math of dit.py:154-168 / torch SDPA)."""
+    qf, kf, vf = q.float().transpose(0, 1), k.float().transpose(0, 1), v.float().transpose(0, 1)
+    s = (qf @ kf.transpose(1, 2)) / math.sqrt(q.shape[-1])
+    o = torch.softmax(s, dim=-1) @ vf
+    return o.transpose(0, 1).reshape(q.shape[0], -1).to(q.dtype)
+
+
+def fp8_linear(xq, xs, w):
+    """Fp8Linear.forward on already-quantised input (fp8_linear.py:139-141); w has wq, ws, bias."""
+    return fp8_scaled_mm(xq, w.wq, xs, w.ws, w.bias, torch.bfloat16)
+
+
+def block_stream_out(x, attn, w, m, eps=1e-6):
+    """Second half of one stream of MMDoubleStreamBlock.forward (dit.py:525-538), FP8 path."""
+    gate1, shift2, scale2, gate2 = m[2], m[3], m[4], m[5]
+    aq, asc = per_token_quant_fp8(attn)
+    proj = fp8_linear(aq, asc, w.proj)
+    h, y = gated_residual_norm_scale_shift(x, proj, gate1, scale2, shift2, "layer", eps)
+    hq, hs = per_token_quant_fp8(y)
+    up = fp8_linear(hq, hs, w.up)
+    gq, gs = per_token_quant_fp8(gelu_tanh(up))
+    down = fp8_linear(gq, gs, w.down)
+    return gated_residual(h, down, gate2)
+
+
+def block_forward(img, txt, vec, cos, sin, w, cache_k, cache_v, heads, eps=1e-6):
+    """MMDoubleStreamBlock.forward for one chunk (dit.py:360-558), FP8 path, composed of the
+    oracle ops above; cache_k/v: token-major [cache_len, H, D] (post-RoPE)."""
+    def mod(table):
+        m = (table + vec)
+        return [m[i:i + 1] for i in range(6)]
+
+    mi, mt = mod(w.img.mod_table), mod(w.txt.mod_table)
+    outs = []
+    for x, ws, m, rope in ((img, w.img, mi, True), (txt, w.txt, mt, False)):
+        xq, xs = norm_scale_shift_quant_fp8(x, None, None, m[1], m[0], "layer", eps)
+        qkv = fp8_linear(xq, xs, ws.qkv)
+        if rope:
+            outs.append(qkv_norm_rope_pack(qkv, heads, ws.q_norm, ws.k_norm, cos, sin, eps, head_major=False))
+        else:
+            outs.append(qkv_text_pack(qkv, heads, ws.q_norm, ws.k_norm, eps))
+    (qi, ki, vi), (qt, kt, vt) = outs
+    attn = attention(torch.cat([qi, qt]), torch.cat([cache_k, ki, kt]), torch.cat([cache_v, vi, vt]))
+    L = img.shape[0]
+    return block_stream_out(img, attn[:L], w.img, mi, eps), block_stream_out(txt, attn[L:], w.txt, mt, eps)
+
+
 # ----------------------------------------------------------------------------- helpers
 def bf16_ulp(x: torch.Tensor) -> torch.Tensor:
     """Spacing of bf16 numbers at |x| (1 ulp of the value), as fp32."""

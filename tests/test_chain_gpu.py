@@ -1,0 +1,171 @@
+"""GPU parity of the per-block chain and the fused ops it adds.
+
+Stage by stage, each op of joyomni_ops.chain.block_forward is checked against the
+oracle applied to the GPU's own inputs of that stage (the per-op tolerances of
+the other test files); end to end, the block output is checked against the
+oracle chain (oracle.ops.block_forward) with the north-star FP8 gate (relative
+Frobenius error <= 2e-2): every FP8 requantisation can move an element by one
+e4m3 step when its bf16 input differs by one ulp, so bit-level agreement is
+only meaningful stage by stage.
+"""
+import pytest
+import torch
+
+from conftest import assert_ulp_close
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def rand(shape, seed, scale=1.0, mean=0.0):
+    g = torch.Generator().manual_seed(seed)
+    return (mean + scale * torch.randn(*shape, generator=g)).to(BF)
+
+
+def rel_err(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def gemm_close(out, ref, what):
+    o, r = out.float().cpu(), ref.float().cpu()
+    rms = r.pow(2).mean().sqrt().item()
+    ulp = torch.pow(2.0, torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
+    bad = (o - r).abs() > 2 * ulp + rms * 2.0 ** -12
+    assert not bad.any(), f"{what}: {bad.sum().item()} elements off"
+
+
+def quant_matches(q, s, y):
+    """(q, s) == per_token_quant(y) bit-exactly."""
+    rq, rs = ops.per_token_quant_fp8(y.cpu())
+    return torch.equal(s.cpu().reshape(-1), rs.reshape(-1)) and torch.equal(q.cpu().view(torch.uint8),
+                                                                             rq.view(torch.uint8))
+
+
+# ------------------------------------------------------------------ new fused ops
+@pytest.mark.parametrize("L,H", [(512, 24), (37, 3)])
+def test_text_pack(jo, dev, L, H):
+    qkv = rand((L, 3 * H * 128), 1)
+    qw, kw = rand((128,), 2, 0.02, 1.0), rand((128,), 3, 0.5, 1.0)
+    q, k, v = jo.qkv_norm_rope_pack(qkv.to(dev), H, qw.to(dev), kw.to(dev), None, None, 1e-6, False)
+    rq, rk, rv = ops.qkv_text_pack(qkv, H, qw, kw, 1e-6)
+    assert torch.equal(v.cpu(), rv)
+    # double rounding: a 1-ulp flip of bf16(x*r) becomes |w| ulps of the output
+    assert assert_ulp_close(q, rq, 2.0, what="text q") > 0.99
+    assert assert_ulp_close(k, rk, 4.0, what="text k") > 0.99
+
+
+def test_pack_into_buffer_slices(jo, dev):
+    L, H = 300, 4
+    qkv = rand((L, 3 * H * 128), 4)
+    qw, kw = rand((128,), 5, 0.02, 1.0), rand((128,), 6, 0.02, 1.0)
+    from joyomni_ops import rope
+
+    cos, sin = rope.video_chunk_tables(3, 10, 10, 2)
+    Q = torch.full((L + 50, H, 128), 7.0, dtype=BF, device=dev)
+    K = torch.full((100 + L + 50, H, 128), 7.0, dtype=BF, device=dev)
+    V = torch.full_like(K, 7.0)
+    jo.qkv_norm_rope_pack_into(qkv.to(dev), H, qw.to(dev), kw.to(dev), cos.to(dev), sin.to(dev), Q[:L],
+                               K[100:100 + L], V[100:100 + L])
+    rq, rk, rv = ops.qkv_norm_rope_pack(qkv, H, qw, kw, cos, sin, 1e-6, head_major=False)
+    assert torch.equal(V[100:100 + L].cpu(), rv)
+    assert_ulp_close(Q[:L], rq, 1.0, what="q")
+    assert_ulp_close(K[100:100 + L], rk, 1.0, what="k")
+    for t, rows in ((Q, slice(L, None)), (K, slice(0, 100)), (K, slice(100 + L, None)), (V, slice(0, 100))):
+        assert (t[rows] == 7.0).all(), "write outside the target rows"
+
+
+@pytest.mark.parametrize("M,N", [(10800, 12288), (512, 12288), (5, 3072), (3, 100)])
+def test_gelu_quant(jo, dev, M, N):
+    x = rand((M, N), 7, 2.0)
+    xg = x.to(dev)
+    q, s = jo.gelu_quant_fp8(xg)
+    y = jo.gelu_tanh(xg)  # same GELU arithmetic: the exact bf16 intermediate of the fused op
+    assert quant_matches(q, s, y)
+    # against the full oracle: bit-exact on every row whose bf16 GELU matches torch's
+    ry = ops.gelu_tanh(x)
+    same = (y.cpu() == ry).all(dim=1)
+    rq, rs = ops.per_token_quant_fp8(ry)
+    assert torch.equal(q.cpu()[same].view(torch.uint8), rq[same].view(torch.uint8))
+    assert torch.equal(s.cpu()[same], rs[same])
+
+
+@pytest.mark.parametrize("M,N", [(10800, 3072), (512, 3072), (7, 4096)])
+def test_gated_residual_norm_quant(jo, dev, M, N):
+    res, x = rand((M, N), 8), rand((M, N), 9)
+    gate, scale, shift = rand((1, N), 10, 0.1), rand((1, N), 11, 0.1), rand((1, N), 12, 0.1)
+    g = lambda t: t.to(dev)
+    h, q, s = jo.gated_residual_norm_scale_shift_quant_fp8(g(res), g(x), g(gate), g(scale), g(shift), "layer", 1e-6)
+    assert_ulp_close(h, ops.gated_residual(res, x, gate), 1.0, what="h")
+    _, y = jo.gated_residual_norm_scale_shift(g(res), g(x), g(gate), g(scale), g(shift), "layer", 1e-6)
+    assert quant_matches(q, s, y)
+    assert_ulp_close(y, ops.norm_scale_shift(h.cpu(), None, None, scale, shift, "layer", 1e-6), 1.0, what="y")
+
+
+# ------------------------------------------------------------------ the chain
+class CpuLinear:
+    def __init__(self, w):
+        self.wq, self.ws = w.wq.cpu(), w.ws.cpu()
+        self.bias = None if w.bias is None else w.bias.cpu()
+
+
+class CpuStream:
+    def __init__(self, s):
+        self.mod_table, self.q_norm, self.k_norm = s.mod_table.cpu(), s.q_norm.cpu(), s.k_norm.cpu()
+        self.qkv, self.proj, self.up, self.down = (CpuLinear(w) for w in (s.qkv, s.proj, s.up, s.down))
+
+
+class CpuBlock:
+    def __init__(self, w):
+        self.img, self.txt = CpuStream(w.img), CpuStream(w.txt)
+
+
+@pytest.mark.parametrize("hidden,heads,ffn,img_len,txt_len,cache_len", [(256, 2, 1024, 96, 16, 32),
+                                                                       (384, 3, 768, 200, 24, 100)])
+def test_block_chain(dev, hidden, heads, ffn, img_len, txt_len, cache_len):
+    from joyomni_ops import chain, rope
+
+    w = chain.random_block_weights(hidden, heads, ffn, device=dev, seed=3)
+    img, txt = rand((img_len, hidden), 20), rand((txt_len, hidden), 21)
+    vec = rand((6, hidden), 22, 0.1)
+    cos, sin = rope.video_chunk_tables(1, 8, img_len // 8, 5)
+    bufs = chain.KVBuffers(cache_len, img_len, txt_len, heads, 128, 1, dev)
+    ck, cv = rand((cache_len, heads, 128), 23), rand((cache_len, heads, 128), 24)
+    bufs.k[:cache_len].copy_(ck)
+    bufs.v[:cache_len].copy_(cv)
+    tr = {}
+    img_out, txt_out = chain.block_forward(img.to(dev), txt.to(dev), vec.to(dev), cos.to(dev), sin.to(dev), w,
+                                           bufs, trace=tr)
+    torch.cuda.synchronize()
+    T = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in tr.items()}
+    W = CpuBlock(w)
+    L = img_len
+    # --- stage by stage, each against the oracle on the GPU's own stage inputs
+    for tag, x, ws, m in (("img", img, W.img, T["mi"]), ("txt", txt, W.txt, T["mt"])):
+        m = [r.cpu() for r in m]
+        xq, xs = ops.norm_scale_shift_quant_fp8(x, None, None, m[1], m[0], "layer", 1e-6)
+        same = (xs.reshape(-1) == T[f"{tag}.xs"].reshape(-1))
+        assert same.float().mean() > 0.9, f"{tag}: LN+quant scales"
+        gemm_close(T[f"{tag}.qkv"], ops.fp8_linear(T[f"{tag}.xq"], T[f"{tag}.xs"], ws.qkv), f"{tag} qkv")
+        assert quant_matches(T[f"{tag}.aq"], T[f"{tag}.as"], T[f"{tag}.attn"])
+        gemm_close(T[f"{tag}.proj"], ops.fp8_linear(T[f"{tag}.aq"], T[f"{tag}.as"], ws.proj), f"{tag} proj")
+        assert_ulp_close(T[f"{tag}.h"], ops.gated_residual(x, T[f"{tag}.proj"], m[2]), 1.0, what=f"{tag} h")
+        gemm_close(T[f"{tag}.up"], ops.fp8_linear(T[f"{tag}.hq"], T[f"{tag}.hs"], ws.up), f"{tag} up")
+        gemm_close(T[f"{tag}.down"], ops.fp8_linear(T[f"{tag}.gq"], T[f"{tag}.gs"], ws.down), f"{tag} down")
+        assert_ulp_close(T[f"{tag}.out"], ops.gated_residual(T[f"{tag}.h"], T[f"{tag}.down"], m[5]), 1.0,
+                         what=f"{tag} out")
+    q_img, k_img, v_img = ops.qkv_norm_rope_pack(T["img.qkv"], heads, W.img.q_norm, W.img.k_norm, cos, sin, 1e-6,
+                                                 head_major=False)
+    q_txt, k_txt, v_txt = ops.qkv_text_pack(T["txt.qkv"], heads, W.txt.q_norm, W.txt.k_norm, 1e-6)
+    assert_ulp_close(T["q"][:L], q_img, 1.0, what="q img")
+    assert_ulp_close(T["k"][cache_len:cache_len + L], k_img, 1.0, what="k img")
+    assert torch.equal(T["v"][cache_len:cache_len + L], v_img)
+    assert_ulp_close(T["q"][L:], q_txt, 4.0, what="q txt")
+    assert torch.equal(T["v"][cache_len + L:], v_txt)
+    assert torch.equal(T["k"][:cache_len], ck) and torch.equal(T["v"][:cache_len], cv)
+    attn_ref = ops.attention(T["q"], T["k"], T["v"])
+    assert rel_err(torch.cat([T["img.attn"], T["txt.attn"]]), attn_ref) < 1e-2
+    # --- end to end against the oracle chain
+    r_img, r_txt = ops.block_forward(img, txt, vec, cos, sin, W, ck, cv, heads)
+    assert rel_err(img_out, r_img) < 2e-2 and rel_err(txt_out, r_txt) < 2e-2

@@ -1,0 +1,98 @@
+"""Host logic of the sequence-parallel chain on CPU ranks (gloo, world_size 2).
+
+Checks the token sharding and the in-place K/V all-gather placement of
+joyomni_ops.chain (which on GPUs runs over NCCL), plus the failure path: a rank
+that never joins the collective makes the others fail with an error instead of
+hanging (short process-group timeout).
+"""
+import datetime
+import os
+import socket
+import sys
+import traceback
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        sys.path[:0] = [str(REPO), str(REPO / "joyai-video-edit_b200")]
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        timeout = datetime.timedelta(seconds=5 if mode == "absent" else 60)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
+        from joyomni_ops import chain
+
+        cache, img, txt, H, D = 6, 8, 3, 2, 4
+        b0, b1 = chain.shard_range(img, world, rank)
+        assert (b1 - b0) * world == img
+        bufs = chain.KVBuffers(cache, img, txt, H, D, world, "cpu", dtype=torch.float32)
+        bufs.k.fill_(-1.0)
+        bufs.v.fill_(-2.0)
+        # each rank writes its own token rows: value = global token index (+0.5 for v)
+        tok = torch.arange(b0, b1, dtype=torch.float32).view(-1, 1, 1).expand(-1, H, D)
+        bufs.k[bufs.img_kv_rows(rank)] = tok
+        bufs.v[bufs.img_kv_rows(rank)] = tok + 0.5
+        if mode == "absent" and rank == 1:
+            q.put((rank, "skipped"))
+            return  # never joins the collective
+        chain.gather_chunk_kv(bufs, rank, None)
+        full = torch.arange(img, dtype=torch.float32).view(-1, 1, 1).expand(-1, H, D)
+        assert torch.equal(bufs.k[bufs.chunk_kv_rows()], full)
+        assert torch.equal(bufs.v[bufs.chunk_kv_rows()], full + 0.5)
+        assert (bufs.k[:cache] == -1).all() and (bufs.k[bufs.txt_kv_rows()] == -1).all()
+        q.put((rank, "ok"))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        q.put((rank, f"error: {type(e).__name__}: {e}\n{traceback.format_exc(limit=2)}"))
+
+
+def _run(mode, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    res = {}
+    while not q.empty():
+        r, msg = q.get()
+        res[r] = msg
+    return res, alive
+
+
+def test_shard_range():
+    sys.path[:0] = [str(REPO / "joyai-video-edit_b200")]
+    from joyomni_ops import chain
+
+    assert chain.shard_range(10800, 8, 7) == (9450, 10800)
+    with pytest.raises(ValueError):
+        chain.shard_range(10801, 2, 0)
+
+
+def test_kv_gather_two_ranks():
+    res, alive = _run("ok")
+    assert not alive and res == {0: "ok", 1: "ok"}, res
+
+
+def test_absent_rank_fails_cleanly():
+    res, alive = _run("absent")
+    assert not alive, "a rank hung"
+    assert res.get(1) == "skipped"
+    assert res.get(0, "").startswith("error"), res
