@@ -3,9 +3,9 @@
 //   D[m, n] = out( scale_a[m] * (sum_k A[m, k] * B[k, n]) * scale_b[n] (+ bias[n]) )
 //
 // Replaces joyomni_ops::fp8_scaled_mm (joyomni_ops/csrc/fp8_gemm.cu:1450-1546),
-// whose sm100 path is a CUTLASS collective with 2x2x1 clusters and TMA
-// multicast (:1015-1159).  This kernel is written directly against the
-// sm_100a instructions and uses NO cluster multicast:
+// whose sm100 path is a CUTLASS collective on 2x2x1 thread-block clusters
+// (:1015-1159).  This kernel is written directly against the sm_100a
+// instructions; every CTA loads its own operand tiles (no cross-CTA broadcast):
 //
 //   * persistent: one CTA per SM walks output tiles of 128 x 256;
 //   * warp 0, one lane: TMA producer.  A tile 128 x 128 B and B tile 256 x 128 B
