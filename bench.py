@@ -38,6 +38,7 @@ import torch  # noqa: E402
 METRIC = "achieved HBM GB/s (% of 8 TB/s) per fused op; µs per DiT-block op chain per chunk"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
 BF = torch.bfloat16
 
 
@@ -502,6 +503,21 @@ def time_device(fn, steps: int, world: int):
     return total, statistics.fmean(per)
 
 
+def time_graph(graph, world: int) -> float:
+    """One replay of the captured K steps bracketed by barrier + synchronize, CUDA
+    events on the replaying stream; returns the replay's device time in ms."""
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end)
+
+
 def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
     """The reference's CPU path (oracle port of its PyTorch code) on the host cores."""
     torch.set_num_threads(os.cpu_count() or 1)
@@ -560,16 +576,39 @@ def run_ours(args, wl: Workload):
         wl.world, wl.rank = world, rank
         wl.group = dist.group.WORLD if world > 1 else None
 
-    # two buffer sets, alternated every step: the working set (2 x in + out) is
-    # several times the 126 MB L2, so no step reads what the previous one left
-    # (the block chain's working set is ~2 GB by itself: one set)
-    nsets = 1 if isinstance(wl, Chain) else 2
-    sets = [wl.make(dev, seed=1 + rank * 2 + i) for i in range(nsets)]
-    sets = sets * (2 // nsets)
+    # rotating buffer sets (inputs, and the outputs each step allocates, kept
+    # alive until their set comes round again): the rotating footprint is at
+    # least twice the 126 MB L2, so no step reads or overwrites what the
+    # previous ones left in L2 (the block chain's working set is ~2 GB by
+    # itself: one set)
+    if isinstance(wl, Chain):
+        nsets = 1
+    else:
+        nsets = max(2, min(16, -(-2 * L2_BYTES // wl.algo_bytes())))
+    sets = [wl.make(dev, seed=1 + rank * 16 + i) for i in range(nsets)]
+    ring = [None] * nsets
+
+    def step(i):
+        ring[i % nsets] = wl.step(sets[i % nsets])
+
     torch.cuda.synchronize()
     for i in range(max(args.warmup, 3)):
-        wl.step(sets[i % 2])
+        step(i)
     torch.cuda.synchronize()
+
+    # the timed K steps run as one CUDA graph replay (no host launch gaps between
+    # the kernels); the block chain, which carries NCCL collectives and library
+    # attention, runs eagerly
+    graph = None
+    if not isinstance(wl, Chain):
+        l0 = cabi.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                step(i)
+        launches = cabi.launch_count() - l0  # kernels per replay
+        graph.replay()
+        torch.cuda.synchronize()
 
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
@@ -578,15 +617,24 @@ def run_ours(args, wl: Workload):
     t_end = time.perf_counter() + 1.0
     i = 0
     while time.perf_counter() < t_end:
-        wl.step(sets[i % 2])
+        if graph is not None:
+            graph.replay()
+        else:
+            step(i)
         i += 1
-        if i % 64 == 0:
+        if i % 16 == 0:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
-    l0 = cabi.launch_count()
-    total_ms, per_ms = time_device(lambda i: wl.step(sets[i % 2]), args.steps, world)
-    launches = cabi.launch_count() - l0
+    if graph is not None:
+        total_ms = time_graph(graph, world)
+        per_ms = total_ms / args.steps
+    else:
+        l0 = cabi.launch_count()
+        total_ms, per_ms = time_device(step, args.steps, world)
+        launches = cabi.launch_count() - l0
     clk = clocks.stop() if clocks else None
+    del graph
+    sets = sets[:2] if len(sets) >= 2 else sets * 2
 
     # end to end through the public op with host (pinned) buffers
     hosts = [wl.make_host(s) for s in sets]
@@ -622,7 +670,9 @@ def run_ours(args, wl: Workload):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "pct_of_8TBs": round(100.0 * value / world / NOMINAL_HBM_GBS, 2),
         "config": {"workload": wl.desc, **wl.shape, "algo_bytes_per_step": B,
-                   "l2": "inputs larger than L2: 2 rotating buffer sets of in+out, each > 126 MB",
+                   "l2": f"{nsets} rotating buffer sets of inputs + outputs, >= 2x the 126 MB L2 in total",
+                   "timing": "K steps captured in one CUDA graph, one replay timed with CUDA events"
+                   if not isinstance(wl, Chain) else "K eager steps, CUDA events",
                    "parallelism": f"{world} independent token partitions (one chunk per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",

@@ -40,13 +40,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps (no issue slots) until
+// the phase completes or the hint elapses, instead of spinning.
+constexpr uint32_t kSuspendNs = 1000000;  // 1 ms
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase of the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* fault) {
-  if (mbar_try(bar, parity)) return true;
+  if (mbar_try_sleep(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 255) == 0 && globaltimer() - t0 > kWaitNs) {
+  for (;;) {
+    if (mbar_try_sleep(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) {
       atomicAdd(fault, 1u);
       return false;
     }
@@ -64,6 +78,18 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
                : "memory");
+}
+// 1-D bulk copy shared -> global (16-byte aligned, size a multiple of 16) in
+// this thread's current bulk async-group.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every bulk store this thread committed has finished reading its
+// shared-memory source (the slot may then be refilled).
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;

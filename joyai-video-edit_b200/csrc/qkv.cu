@@ -198,17 +198,34 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
 // Staged variant (B200 fast path).  Unit = all heads of one token for one of
 // q/k/v (kPack: a contiguous H*D slice of the qkv row) or for q/k (kInPlace: a
 // contiguous token row of q or k).  Each warp owns kQkSlots shared-memory
-// slots and feeds itself with 1-D TMA bulk copies: when a unit lands the warp
-// pulls it into registers (D/8 lanes per head, 16 bytes per lane), refills the
-// slot with its unit kQkSlots ahead, then normalises + rotates with packed
-// fp32 (f32x2) arithmetic and stores 2*D-byte rows.  The head rsqrt uses the
-// hardware approximation (rel. error ~2^-22, far below the bf16 output ulp).
+// slots and feeds itself with 1-D TMA bulk copies.
+//   v units (kPack): never enter registers -- each head row goes from the slot
+//     to its destination with one 2*D-byte bulk store (shared -> global).
+//   q/k units: the warp pulls the unit into registers (D/8 lanes per head, 16
+//     bytes per lane), refills the slot with its unit kQkSlots ahead, then
+//     normalises + rotates with packed fp32 (f32x2) arithmetic and stores
+//     2*D-byte rows.
+// Rotation with the norm weight folded in, per pair (x0, x1) of a head row:
+//   out = r * (x0 * (w0 c, w0 s) + x1 * (-w1 s, w1 c))
+// where the four per-lane products depend only on the token (c, s) and the
+// lane (w), so they are formed once per unit.  Vectors hold the even / odd
+// elements of two adjacent pairs, so no operand needs a broadcast.  The head
+// rsqrt uses the hardware approximation (rel. error ~2^-22, far below the bf16
+// output ulp); the regrouped products move the fp32 result by a few fp32 ulps
+// (at most one bf16 ulp after rounding).
 constexpr int kQkWarps = 16;
 constexpr int kQkSlots = 2;
 constexpr int kQkMaxIt = 16;  // head iterations held in registers (H <= 16 * 32/(D/8))
 
 __device__ __forceinline__ float2 bf2f(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+// (lo(a), lo(b)) and (hi(a), hi(b)): even / odd elements of two bf16 pairs
+__device__ __forceinline__ float2 bf_lo2(uint32_t a, uint32_t b) {
+  return make_float2(__uint_as_float(a << 16), __uint_as_float(b << 16));
+}
+__device__ __forceinline__ float2 bf_hi2(uint32_t a, uint32_t b) {
+  return make_float2(__uint_as_float(a & 0xffff0000u), __uint_as_float(b & 0xffff0000u));
 }
 
 template <int kD, int kMode, bool kPre, bool kRope>
@@ -254,15 +271,14 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
   };
   if (lane == 0)
     for (int kk = 0; kk < kQkSlots; ++kk) issue(kk);
-  float2 wq[4], wk[4];
+  // norm weights of this lane's 4 pairs as (even, odd) vectors of pair groups 0 / 1
+  float2 wq0[2], wq1[2], wk0[2], wk1[2];
   {
     const uint4 q4 = ld_bcast(a.qw + j * 8), k4 = ld_bcast(a.kw + j * 8);
-    const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w}, kw[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      wq[e] = bf2f(qw[e]);
-      wk[e] = bf2f(kw[e]);
-    }
+    wq0[0] = bf_lo2(q4.x, q4.y), wq1[0] = bf_hi2(q4.x, q4.y);
+    wq0[1] = bf_lo2(q4.z, q4.w), wq1[1] = bf_hi2(q4.z, q4.w);
+    wk0[0] = bf_lo2(k4.x, k4.y), wk1[0] = bf_hi2(k4.x, k4.y);
+    wk0[1] = bf_lo2(k4.z, k4.w), wk1[1] = bf_hi2(k4.z, k4.w);
   }
   const float inv_d = 1.0f / (float)kD;  // exact for power-of-two D
   int kk = 0;
@@ -271,21 +287,41 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
     int64_t tok;
     int part;
     __nv_bfloat16* unit_dst = unit_ptr(i, tok, part);  // kInPlace destination
-    float2 cs[4], ns[4];  // (c, s) and (-s, c) per rotated pair
-    if (kRope && part < 2) {
+    const uint32_t bar = bar0 + 8u * (uint32_t)(kk % kQkSlots);
+    const uint32_t sl = slot0 + (uint32_t)(kk % kQkSlots) * slot_bytes;
+    if constexpr (kMode == kPack) {
+      if (part == 2) {
+        if (!mbar_wait(bar, (uint32_t)((kk / kQkSlots) & 1), fault)) break;
+        __nv_bfloat16* vdst = a.out[2] + tok * a.os_t;
+        for (int h = lane; h < H; h += 32) bulk_store(vdst + (int64_t)h * a.os_h, sl + (uint32_t)h * kD * 2u, kD * 2u);
+        bulk_commit();
+        bulk_wait_read_all();
+        __syncwarp();
+        if (lane == 0) issue(kk + kQkSlots);
+        continue;
+      }
+    }
+    float2 w0[2], w1[2];  // selected by value: a pointer select would put the arrays on the stack
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      w0[g] = part == 0 ? wq0[g] : wk0[g];
+      w1[g] = part == 0 ? wq1[g] : wk1[g];
+    }
+    // folded rotation operands of pair groups 0 / 1: A = W0*C, B = -W1*S, C' = W0*S, D' = W1*C
+    float2 fa[2], fb[2], fc[2], fd[2];
+    if constexpr (kRope) {
       const int64_t rt = kMode == kPack ? tok : tok % a.seq_len;
       const uint2 c2 = __ldg(reinterpret_cast<const uint2*>(a.cos + rt * (kD / 2) + j * 4));
       const uint2 s2 = __ldg(reinterpret_cast<const uint2*>(a.sin + rt * (kD / 2) + j * 4));
-      const float2 c01 = bf2f(c2.x), c23 = bf2f(c2.y), s01 = bf2f(s2.x), s23 = bf2f(s2.y);
-      const float c[4] = {c01.x, c01.y, c23.x, c23.y}, sn[4] = {s01.x, s01.y, s23.x, s23.y};
+      const float2 c[2] = {bf2f(c2.x), bf2f(c2.y)}, s[2] = {bf2f(s2.x), bf2f(s2.y)};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        cs[e] = make_float2(c[e], sn[e]);
-        ns[e] = make_float2(-sn[e], c[e]);
+      for (int g = 0; g < 2; ++g) {
+        fa[g] = __fmul2_rn(w0[g], c[g]);
+        fb[g] = __fmul2_rn(make_float2(-w1[g].x, -w1[g].y), s[g]);
+        fc[g] = __fmul2_rn(w0[g], s[g]);
+        fd[g] = __fmul2_rn(w1[g], c[g]);
       }
     }
-    const uint32_t bar = bar0 + 8u * (uint32_t)(kk % kQkSlots);
-    const uint32_t sl = slot0 + (uint32_t)(kk % kQkSlots) * slot_bytes;
     if (!mbar_wait(bar, (uint32_t)((kk / kQkSlots) & 1), fault)) break;
     uint4 v[kQkMaxIt];
 #pragma unroll
@@ -298,87 +334,91 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // reads before the refill
       issue(kk + kQkSlots);
     }
-    const float2* w = part == 0 ? wq : wk;
+    // destination of head row sub (+ kHPI per iteration), this lane's 16 bytes
+    __nv_bfloat16* dst;
+    int64_t step;
+    if constexpr (kMode == kPack) {
+      dst = a.out[part] + tok * a.os_t + (int64_t)sub * a.os_h + j * 8;
+      step = (int64_t)kHPI * a.os_h;
+    } else {
+      dst = unit_dst + sub * kD + j * 8;
+      step = (int64_t)kHPI * kD;
+    }
+    __nv_bfloat16* pre = nullptr;  // pre-RoPE k, laid out as k
+    if constexpr (kPre) {
+      if (part == 1) pre = a.k_pre + (kMode == kPack ? dst - a.out[1] : dst - a.k);
+    }
     // groups of 4 head iterations, phase-major, so the 4 shuffle + rsqrt
     // dependency chains of a group overlap
 #pragma unroll
     for (int g0 = 0; g0 < kQkMaxIt; g0 += 4) {
       if (g0 >= NI) break;  // uniform across the warp
+      float2 e[4][2], o[4][2];
       float ss[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint4 u = v[g0 + q];
-        float2 p0 = bf2f(u.x), p1 = bf2f(u.y), p2 = bf2f(u.z), p3 = bf2f(u.w);
-        float2 acc = __fmul2_rn(p0, p0);
-        acc = __ffma2_rn(p1, p1, acc);
-        acc = __ffma2_rn(p2, p2, acc);
-        acc = __ffma2_rn(p3, p3, acc);
-        ss[q] = (g0 + q < NI) ? acc.x + acc.y : 0.f;
+        e[q][0] = bf_lo2(u.x, u.y), o[q][0] = bf_hi2(u.x, u.y);
+        e[q][1] = bf_lo2(u.z, u.w), o[q][1] = bf_hi2(u.z, u.w);
+        float2 acc = __fmul2_rn(e[q][0], e[q][0]);
+        acc = __ffma2_rn(o[q][0], o[q][0], acc);
+        acc = __ffma2_rn(e[q][1], e[q][1], acc);
+        acc = __ffma2_rn(o[q][1], o[q][1], acc);
+        ss[q] = acc.x + acc.y;
       }
 #pragma unroll
-      for (int o = kTPH / 2; o > 0; o >>= 1)  // every lane, before any divergence
+      for (int off = kTPH / 2; off > 0; off >>= 1)  // every lane, before any divergence
 #pragma unroll
-        for (int q = 0; q < 4; ++q) ss[q] += __shfl_xor_sync(0xffffffffu, ss[q], o);
+        for (int q = 0; q < 4; ++q) ss[q] += __shfl_xor_sync(0xffffffffu, ss[q], off);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int it = g0 + q;
-        const int h = it * kHPI + sub;
-        if (it >= NI || h >= H) continue;
-        int64_t off;
-        __nv_bfloat16* dst;
-        if constexpr (kMode == kPack) {
-          off = (int64_t)h * a.os_h + tok * a.os_t + j * 8;
-          dst = part == 0 ? a.out[0] : (part == 1 ? a.out[1] : a.out[2]);
-        } else {
-          off = (int64_t)h * kD + j * 8;
-          dst = unit_dst;
-        }
-        if (part == 2) {
-          st_global(dst + off, v[it]);
-          continue;
-        }
-        const uint32_t u[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
-        float2 p[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) p[e] = bf2f(u[e]);
+        if (it >= NI || it * kHPI + sub >= H) continue;
         const float r = rsqrtf(fmaf(ss[q], inv_d, a.eps));
         const float2 r2 = make_float2(r, r);
+        __nv_bfloat16* d = dst + it * step;
+        uint32_t o4[4];
         if constexpr (!kRope) {
           // text rows: the model's RMSNorm rounds twice, bf16(x * r) then bf16(. * w)
-          uint32_t o4[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 nrm = bf2f(pack_bf16x2(__fmul_rn(p[e].x, r), __fmul_rn(p[e].y, r)));
-            const float2 y = __fmul2_rn(nrm, w[e]);
-            o4[e] = pack_bf16x2(y.x, y.y);
+          for (int g = 0; g < 2; ++g) {
+            const uint32_t n0 = pack_bf16x2(__fmul_rn(e[q][g].x, r), __fmul_rn(o[q][g].x, r));
+            const uint32_t n1 = pack_bf16x2(__fmul_rn(e[q][g].y, r), __fmul_rn(o[q][g].y, r));
+            const float2 ye = __fmul2_rn(bf_lo2(n0, n1), w0[g]), yo = __fmul2_rn(bf_hi2(n0, n1), w1[g]);
+            o4[2 * g] = pack_bf16x2(ye.x, yo.x);
+            o4[2 * g + 1] = pack_bf16x2(ye.y, yo.y);
           }
           if constexpr (kPre) {
-            if (part == 1) {
-              const int64_t pre = kMode == kPack ? off : tok * (int64_t)H * kD + off;
-              st_global(a.k_pre + pre, make_uint4(o4[0], o4[1], o4[2], o4[3]));
-            }
+            if (part == 1) st_global(pre + it * step, make_uint4(o4[0], o4[1], o4[2], o4[3]));
           }
-          st_global(dst + off, make_uint4(o4[0], o4[1], o4[2], o4[3]));
+          st_global(d, make_uint4(o4[0], o4[1], o4[2], o4[3]));
           continue;
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) p[e] = __fmul2_rn(__fmul2_rn(p[e], r2), w[e]);  // (x * r) * w
+        for (int g = 0; g < 2; ++g) {
+          e[q][g] = __fmul2_rn(e[q][g], r2);
+          o[q][g] = __fmul2_rn(o[q][g], r2);
+        }
         if constexpr (kPre) {
-          if (part == 1) {
-            const int64_t pre = kMode == kPack ? off : tok * (int64_t)H * kD + off;
-            st_global(a.k_pre + pre, make_uint4(pack_bf16x2(p[0].x, p[0].y), pack_bf16x2(p[1].x, p[1].y),
-                                                pack_bf16x2(p[2].x, p[2].y), pack_bf16x2(p[3].x, p[3].y)));
+          if (part == 1) {  // pre-RoPE k: (x * r) * w
+            uint32_t p4[4];
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              const float2 ye = __fmul2_rn(e[q][g], w0[g]), yo = __fmul2_rn(o[q][g], w1[g]);
+              p4[2 * g] = pack_bf16x2(ye.x, yo.x);
+              p4[2 * g + 1] = pack_bf16x2(ye.y, yo.y);
+            }
+            st_global(pre + it * step, make_uint4(p4[0], p4[1], p4[2], p4[3]));
           }
         }
-        uint32_t o4[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          // (x0 c - x1 s, x0 s + x1 c) = x1 * (-s, c) + x0 * (c, s)
-          const float2 t = __fmul2_rn(make_float2(p[e].x, p[e].x), cs[e]);
-          const float2 rr = __ffma2_rn(make_float2(p[e].y, p[e].y), ns[e], t);
-          o4[e] = pack_bf16x2(rr.x, rr.y);
+        for (int g = 0; g < 2; ++g) {
+          const float2 y0 = __ffma2_rn(o[q][g], fb[g], __fmul2_rn(e[q][g], fa[g]));  // x0 w0 c - x1 w1 s
+          const float2 y1 = __ffma2_rn(o[q][g], fd[g], __fmul2_rn(e[q][g], fc[g]));  // x0 w0 s + x1 w1 c
+          o4[2 * g] = pack_bf16x2(y0.x, y1.x);
+          o4[2 * g + 1] = pack_bf16x2(y0.y, y1.y);
         }
-        st_global(dst + off, make_uint4(o4[0], o4[1], o4[2], o4[3]));
+        st_global(d, make_uint4(o4[0], o4[1], o4[2], o4[3]));
       }
     }
   }

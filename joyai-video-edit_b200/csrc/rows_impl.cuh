@@ -12,13 +12,13 @@
 //
 // Design (B200): the ops are HBM-bound, so each row is read from HBM exactly
 // once, kept in registers across the reduction(s), and written once with
-// 16-byte stores.  Rows of up to 512 vectors (4096 bf16) stream through a
-// shared-memory ring filled by 1-D TMA bulk copies (one producer warp, eight
-// consumer warps, one row per consumer at a time, reductions by warp shuffle):
-// the loads in flight are held by the copy engine, not by registers, so each
-// SM keeps ~192 KB of rows in flight while its warps compute.  Longer rows are
-// owned by a CTA with direct 16-byte loads; shapes that break 16-byte
-// alignment take a scalar block-per-row path.
+// 16-byte stores.  Rows of up to 512 vectors (4096 bf16) stream through
+// shared memory: every warp owns a few row slots that it refills itself with
+// 1-D TMA bulk copies (the loads in flight are held by the copy engine, not by
+// registers), reductions are warp shuffles / warp reduce instructions, and
+// broadcast operands are cached per CTA as fp32.  Longer rows, or per-row
+// modulation / gate operands, are owned by a CTA with direct 16-byte loads;
+// shapes that break 16-byte alignment take a scalar block-per-row path.
 #pragma once
 #include "pipeline.cuh"
 #include "rows_decl.cuh"
@@ -259,159 +259,307 @@ __device__ __forceinline__ float2 div2_markstein(float2 x, float2 s, float2 rc) 
   const float2 q = __ffma2_rn(r, rc, q0);
   return make_float2(copysignf(q.x, x.x), copysignf(q.y, x.y));
 }
+// The same quotient without the sign copy (ns = -s): for 16-bit inputs the
+// sign of x = -0 is restored on the packed e4m3 bytes instead (e4m3_signs),
+// one byte permute for four elements.
+__device__ __forceinline__ float2 div2_ms(float2 x, float2 ns, float2 rc) {
+  const float2 q0 = __fmul2_rn(x, rc);
+  const float2 r = __ffma2_rn(q0, ns, x);
+  return __ffma2_rn(r, rc, q0);
+}
+// Sign bits of the four 16-bit elements of words (w0, w1), at bit 7 of the
+// byte each element's e4m3 code occupies.  OR-ing them in is exact: a nonzero
+// quotient already carries its sign, a zero one gets the sign of x.
+__device__ __forceinline__ uint32_t e4m3_signs(uint32_t w0, uint32_t w1) {
+  return __byte_perm(w0, w1, 0x7531) & 0x80808080u;
+}
+// Running |x| maximum over packed 16-bit floats: bf16 and fp16 magnitudes
+// order exactly as their bit patterns with the sign cleared (unsigned).
+__device__ __forceinline__ uint32_t absmax_u16x2(uint32_t m, uint32_t w) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w & 0x7fff7fffu));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ float bits16_to_f(uint32_t h);
+template <>
+__device__ __forceinline__ float bits16_to_f<__nv_bfloat16>(uint32_t h) {
+  return __uint_as_float(h << 16);
+}
+template <>
+__device__ __forceinline__ float bits16_to_f<__half>(uint32_t h) {
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+template <>
+__device__ __forceinline__ float bits16_to_f<float>(uint32_t) {
+  return 0.f;
+}
 
 // Feature bits of a staged row op (compile-time, no per-element branches).
-enum Feat { kFG = 1, kFB = 2, kFMod = 4 };
+// Every feature is a broadcast row (one [cols] vector for all rows).
+enum Feat { kFG = 1, kFB = 2, kFMod = 4, kFGate = 8 };
+constexpr int kMaxG = 4;  // warps per row group, at most
+
+// Broadcast operands live in shared memory as fp32 so the row math converts
+// nothing for them: one set of 4*cols bytes per present operand, in the order
+// gamma, beta, 1+scale, shift, gate.  Within a set, vector idx (V elements) is
+// V/4 float4 at plane p: set + (p * nvec + idx) * 16, so the float4 reads of a
+// warp (consecutive idx) are contiguous and free of bank conflicts.
+template <int kF>
+struct Sets {
+  static constexpr int g = 0;
+  static constexpr int b = g + ((kF & kFG) ? 1 : 0);
+  static constexpr int c1 = b + ((kF & kFB) ? 1 : 0);
+  static constexpr int sh = c1 + ((kF & kFMod) ? 1 : 0);
+  static constexpr int gate = sh + ((kF & kFMod) ? 1 : 0);
+  static constexpr int n = gate + ((kF & kFGate) ? 1 : 0);
+};
+
+template <int V>
+__device__ __forceinline__ void ld_set(uint32_t set, int nvec, int idx, float2* p) {
+#pragma unroll
+  for (int pl = 0; pl < V / 4; ++pl) {
+    const uint4 u = lds128(set + (uint32_t)(pl * nvec + idx) * 16u);
+    p[2 * pl] = make_float2(__uint_as_float(u.x), __uint_as_float(u.y));
+    p[2 * pl + 1] = make_float2(__uint_as_float(u.z), __uint_as_float(u.w));
+  }
+}
+
+// Reductions over the warps of a row group: warp shuffle / warp reduce, then
+// (G > 1) the G warp partials through shared memory and the group's named
+// barrier, summed in warp order by every thread (identical results in all
+// warps).  Each kind (0 sum, 1 variance sum, 2 amax) has its own partial slots;
+// every row starts with a group barrier, so no slot is rewritten before all
+// warps have read it.
+struct GroupRed {
+  float* part;  // this group's [3][kMaxG] partials
+  int G, wg, lane, bar_id;
+  __device__ __forceinline__ void sync() const {
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(G * 32) : "memory");
+  }
+  __device__ __forceinline__ float sum(float v, int kind) const {
+    v = warp_sum(v);
+    if (G == 1) return v;
+    float* r = part + kind * kMaxG;
+    if (lane == 0) r[wg] = v;
+    sync();
+    float s = r[0];
+    for (int i = 1; i < G; ++i) s += r[i];
+    return s;
+  }
+  __device__ __forceinline__ uint32_t umax(uint32_t v, int kind) const {
+    v = __reduce_max_sync(0xffffffffu, v);
+    if (G == 1) return v;
+    uint32_t* r = reinterpret_cast<uint32_t*>(part) + kind * kMaxG;
+    if (lane == 0) r[wg] = v;
+    sync();
+    uint32_t s = r[0];
+    for (int i = 1; i < G; ++i) s = max(s, r[i]);
+    return s;
+  }
+  // AND of `v` over the group (every warp of the group must call it)
+  __device__ __forceinline__ bool all(bool v) const {
+    if (G == 1) return __all_sync(0xffffffffu, v);
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(bar_id), "r"(G * 32)
+        : "memory");
+    return r != 0;
+  }
+};
 
 // Row math of the staged path, f32x2 throughout.  Same operation order as
 // row_math (LayerNorm ((x-mean)*rstd*g + b)*(1+sc)+sh, RMS (x*rstd*g)*(1+sc)+sh;
 // two-pass mean/variance; quant on the T-rounded y).
 template <typename T, int kVPT, int kNorm, int kEpi, int kF>
 __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT], int lane,
-                                          float* red) {
+                                          uint32_t cache, int nvec, const GroupRed& red) {
+  const int GT = red.G * 32;  // threads of the row group; this thread's vectors: lane + GT * i
   constexpr int V = Elt<T>::kVec, P = V / 2;
-  const int nvec = (int)(a.cols / V);
+  constexpr bool k16 = V == 8;
+  constexpr bool kIdentity = kNorm == kNoNorm && (kF & (kFG | kFB | kFMod)) == 0;  // y == x
+  using S = Sets<kF>;
+  const uint32_t set_bytes = (uint32_t)nvec * (uint32_t)V * 4u;
   float mean = 0.f, rstd = 1.f;
   if constexpr (kNorm == kLayer) {
-    float2 acc = f2(0.f);
+    float2 s0 = f2(0.f), s1 = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kVPT; ++i)
-      if (lane + 32 * i < nvec) {
+      if (lane + GT * i < nvec) {
         float2 p[P];
         to_pairs<T>(raw[i], p);
 #pragma unroll
-        for (int e = 0; e < P; ++e) acc = __fadd2_rn(acc, p[e]);
-      }
-    mean = __fdiv_rn(warp_sum(acc.x + acc.y), (float)a.cols);
-    const float2 nm = f2(-mean);
-    float2 q = f2(0.f);
-#pragma unroll
-    for (int i = 0; i < kVPT; ++i)
-      if (lane + 32 * i < nvec) {
-        float2 p[P];
-        to_pairs<T>(raw[i], p);
-#pragma unroll
-        for (int e = 0; e < P; ++e) {
-          const float2 d = __fadd2_rn(p[e], nm);
-          q = __ffma2_rn(d, d, q);
+        for (int e = 0; e < P; e += 2) {
+          s0 = __fadd2_rn(s0, p[e]);
+          s1 = __fadd2_rn(s1, p[e + 1]);
         }
       }
-    rstd = rsqrt_ieee(__fdiv_rn(warp_sum(q.x + q.y), (float)a.cols) + a.eps);
-  } else if constexpr (kNorm == kRms) {
-    float2 q = f2(0.f);
+    mean = __fdiv_rn(red.sum((s0.x + s1.x) + (s0.y + s1.y), 0), (float)a.cols);
+    const float2 nm = f2(-mean);
+    float2 q0 = f2(0.f), q1 = f2(0.f);
 #pragma unroll
     for (int i = 0; i < kVPT; ++i)
-      if (lane + 32 * i < nvec) {
+      if (lane + GT * i < nvec) {
         float2 p[P];
         to_pairs<T>(raw[i], p);
 #pragma unroll
-        for (int e = 0; e < P; ++e) q = __ffma2_rn(p[e], p[e], q);
+        for (int e = 0; e < P; e += 2) {
+          const float2 d0 = __fadd2_rn(p[e], nm), d1 = __fadd2_rn(p[e + 1], nm);
+          q0 = __ffma2_rn(d0, d0, q0);
+          q1 = __ffma2_rn(d1, d1, q1);
+        }
       }
-    rstd = rsqrt_ieee(__fdiv_rn(warp_sum(q.x + q.y), (float)a.cols) + a.eps);
+    rstd = rsqrt_ieee(__fdiv_rn(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), (float)a.cols) + a.eps);
+  } else if constexpr (kNorm == kRms) {
+    float2 q0 = f2(0.f), q1 = f2(0.f);
+#pragma unroll
+    for (int i = 0; i < kVPT; ++i)
+      if (lane + GT * i < nvec) {
+        float2 p[P];
+        to_pairs<T>(raw[i], p);
+#pragma unroll
+        for (int e = 0; e < P; e += 2) {
+          q0 = __ffma2_rn(p[e], p[e], q0);
+          q1 = __ffma2_rn(p[e + 1], p[e + 1], q1);
+        }
+      }
+    rstd = rsqrt_ieee(__fdiv_rn(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), (float)a.cols) + a.eps);
   }
-  const float2 nm2 = f2(-mean), r2 = f2(rstd), one2 = f2(1.f);
-  const T* gam = reinterpret_cast<const T*>(a.gamma);
-  const T* bet = reinterpret_cast<const T*>(a.beta);
-  const T* scr = (kF & kFMod) ? reinterpret_cast<const T*>(a.scale) + row * a.mod_stride : nullptr;
-  const T* shr = (kF & kFMod) ? reinterpret_cast<const T*>(a.shift) + row * a.mod_stride : nullptr;
-  float amax = 0.f;
+  const float2 nm2 = f2(-mean), r2 = f2(rstd);
+  uint32_t amax16 = 0u;  // 16-bit types: packed |y| maximum
+  float amaxf = 0.f;     // fp32 rows
 #pragma unroll
   for (int i = 0; i < kVPT; ++i) {
-    const int idx = lane + 32 * i;
+    const int idx = lane + GT * i;
     if (idx >= nvec) continue;
-    float2 y[P];
-    to_pairs<T>(raw[i], y);
-    if constexpr (kNorm == kLayer) {
+    if constexpr (!kIdentity) {
+      float2 y[P];
+      to_pairs<T>(raw[i], y);
+      if constexpr (kNorm == kLayer) {
 #pragma unroll
-      for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(__fadd2_rn(y[e], nm2), r2);
-    } else if constexpr (kNorm == kRms) {
+        for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(__fadd2_rn(y[e], nm2), r2);
+      } else if constexpr (kNorm == kRms) {
 #pragma unroll
-      for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(y[e], r2);
+        for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(y[e], r2);
+      }
+      if constexpr ((kF & kFG) != 0) {
+        float2 g[P];
+        ld_set<V>(cache + S::g * set_bytes, nvec, idx, g);
+#pragma unroll
+        for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(y[e], g[e]);
+      }
+      if constexpr ((kF & kFB) != 0) {
+        float2 b[P];
+        ld_set<V>(cache + S::b * set_bytes, nvec, idx, b);
+#pragma unroll
+        for (int e = 0; e < P; ++e) y[e] = __fadd2_rn(y[e], b[e]);
+      }
+      if constexpr ((kF & kFMod) != 0) {
+        float2 c1[P], sh[P];
+        ld_set<V>(cache + S::c1 * set_bytes, nvec, idx, c1);
+        ld_set<V>(cache + S::sh * set_bytes, nvec, idx, sh);
+#pragma unroll
+        for (int e = 0; e < P; ++e) y[e] = __ffma2_rn(y[e], c1[e], sh[e]);
+      }
+      if constexpr (kEpi == kStoreY) {
+        st_global(reinterpret_cast<T*>(a.out) + row * a.out_stride + (int64_t)idx * V, from_pairs<T>(y));
+        continue;
+      } else {
+        raw[i] = from_pairs<T>(y);  // y rounded to T, as the unfused chain materialises it
+      }
     }
-    // generic loads: these operands may live in shared memory (staged copies)
-    if constexpr ((kF & kFG) != 0) {
-      float2 g[P];
-      to_pairs<T>(*reinterpret_cast<const uint4*>(gam + (int64_t)idx * V), g);
+    if constexpr (kEpi == kQuantY) {
+      if constexpr (k16) {
+        amax16 = absmax_u16x2(amax16, raw[i].x);
+        amax16 = absmax_u16x2(amax16, raw[i].y);
+        amax16 = absmax_u16x2(amax16, raw[i].z);
+        amax16 = absmax_u16x2(amax16, raw[i].w);
+      } else {
+        float f[V];
+        Elt<T>::unpack(raw[i], f);
 #pragma unroll
-      for (int e = 0; e < P; ++e) y[e] = __fmul2_rn(y[e], g[e]);
-    }
-    if constexpr ((kF & kFB) != 0) {
-      float2 b[P];
-      to_pairs<T>(*reinterpret_cast<const uint4*>(bet + (int64_t)idx * V), b);
-#pragma unroll
-      for (int e = 0; e < P; ++e) y[e] = __fadd2_rn(y[e], b[e]);
-    }
-    if constexpr ((kF & kFMod) != 0) {
-      float2 sc[P], sh[P];
-      to_pairs<T>(*reinterpret_cast<const uint4*>(scr + (int64_t)idx * V), sc);
-      to_pairs<T>(*reinterpret_cast<const uint4*>(shr + (int64_t)idx * V), sh);
-#pragma unroll
-      for (int e = 0; e < P; ++e) y[e] = __ffma2_rn(y[e], __fadd2_rn(one2, sc[e]), sh[e]);
-    }
-    if constexpr (kEpi == kStoreY) {
-      st_global(reinterpret_cast<T*>(a.out) + row * a.out_stride + (int64_t)idx * V, from_pairs<T>(y));
-    } else {
-      raw[i] = from_pairs<T>(y);  // y rounded to T, as the unfused chain materialises it
-      float f[V];
-      Elt<T>::unpack(raw[i], f);
-#pragma unroll
-      for (int e = 0; e < V; ++e) amax = fmaxf(amax, fabsf(f[e]));
+        for (int e = 0; e < V; ++e) amaxf = fmaxf(amaxf, fabsf(f[e]));
+      }
     }
   }
   if constexpr (kEpi == kQuantY) {
-    const float s = quant_scale(warp_max(amax));
-    const float2 s2 = f2(s), rc2 = f2(__frcp_rn(s));
+    float amax;
+    if constexpr (k16) {
+      amax = bits16_to_f<T>(red.umax(max(amax16 & 0xffffu, amax16 >> 16), 2));
+    } else {
+      amax = __uint_as_float(red.umax(__float_as_uint(amaxf), 2));  // |y| >= 0: bits order as values
+    }
+    const float s = quant_scale(amax);
+    const float2 s2 = f2(s), ns2 = f2(-s), rc2 = f2(__frcp_rn(s));
     uint8_t* qrow = a.out_q + row * a.q_stride;
 #pragma unroll
     for (int i = 0; i < kVPT; ++i) {
-      const int idx = lane + 32 * i;
+      const int idx = lane + GT * i;
       if (idx >= nvec) continue;
       float2 p[P];
       to_pairs<T>(raw[i], p);
-      uint32_t w[P / 2];
-#pragma unroll
-      for (int e = 0; e < P; e += 2) {
+      if constexpr (k16) {
         // satfinite conversion saturates |q| > 448 to 448, as the reference clamp does
-        const float2 q0 = div2_markstein(p[e], s2, rc2), q1 = div2_markstein(p[e + 1], s2, rc2);
-        w[e / 2] = (uint32_t)e4m3x2(q0.x, q0.y) | ((uint32_t)e4m3x2(q1.x, q1.y) << 16);
+        float2 q[P];
+#pragma unroll
+        for (int e = 0; e < P; ++e) q[e] = div2_ms(p[e], ns2, rc2);
+        const uint32_t w0 = ((uint32_t)e4m3x2(q[0].x, q[0].y) | ((uint32_t)e4m3x2(q[1].x, q[1].y) << 16)) |
+                            e4m3_signs(raw[i].x, raw[i].y);
+        const uint32_t w1 = ((uint32_t)e4m3x2(q[2].x, q[2].y) | ((uint32_t)e4m3x2(q[3].x, q[3].y) << 16)) |
+                            e4m3_signs(raw[i].z, raw[i].w);
+        *reinterpret_cast<uint2*>(qrow + (int64_t)idx * 8) = make_uint2(w0, w1);
+      } else {
+        const float2 q0 = div2_markstein(p[0], s2, rc2), q1 = div2_markstein(p[1], s2, rc2);
+        *reinterpret_cast<uint32_t*>(qrow + (int64_t)idx * 4) =
+            (uint32_t)e4m3x2(q0.x, q0.y) | ((uint32_t)e4m3x2(q1.x, q1.y) << 16);
       }
-      if constexpr (V == 8)
-        *reinterpret_cast<uint2*>(qrow + (int64_t)idx * 8) = make_uint2(w[0], w[1]);
-      else
-        *reinterpret_cast<uint32_t*>(qrow + (int64_t)idx * 4) = w[0];
     }
-    if (lane == 0) a.out_s[row] = s;
+    if (lane == 0) a.out_s[row] = s;  // thread 0 of the group
   }
-  (void)red;
 }
 
 // ------------------------------------------------------------------ staged path
-// Rows of up to 512 vectors (4096 bf16).  Each warp owns `m` shared-memory
-// slots and feeds itself: lane 0 keeps its next m rows in flight with 1-D TMA
-// bulk copies; when a row lands the warp pulls it into registers, refills the
-// slot with the row m ahead, and computes + stores while those copies fly.
-// Warps never wait on each other (no producer warp, no head-of-line blocking),
-// and each slot has a single owner, so its mbarrier is never waited on more
-// than one phase ahead.  Broadcast operands (gamma, beta, and scale/shift when
-// they are one row) are staged once per CTA in shared memory.
-constexpr int kMaxWarps = 16;
+// Rows of up to 512 vectors (4096 bf16).  A row group of G warps (G = 1, 2, 4
+// by row length, so each thread holds at most 4 vectors) owns `m` shared-
+// memory slots and feeds itself: its leader thread keeps the group's next m
+// rows in flight with 1-D TMA bulk copies; when a row lands the G warps pull it
+// into registers, the leader refills the slot with the row m ahead, and the
+// group computes + stores while those copies fly.  32 warps per SM hide the
+// latency of the reductions.  Groups never wait on each other, and each slot
+// has a single owner group whose warps all pass a group barrier before the
+// refill, so no mbarrier is waited on more than one phase ahead.  Broadcast
+// operands (gamma, beta, 1+scale, shift, gate) are staged once per CTA in
+// shared memory as fp32 sets.
+constexpr int kMaxWarps = 32;
+// threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread)
+constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : 512); }
 
 struct StagedCfg {
-  int warps;            // consumer warps per CTA (blockDim.x / 32)
-  int m;                // slots per warp
+  int warps;            // warps per CTA (blockDim.x / 32), a multiple of G
+  int G;                // warps per row group (1, 2 or 4)
+  int m;                // slots per group
   uint32_t slot_bytes;  // >= one row (two for kResidGate)
-  uint32_t cache_off;   // byte offset of the broadcast-vector cache
+  uint32_t red_off;     // byte offset of the groups' reduction partials
+  uint32_t cache_off;   // byte offset of the broadcast-operand sets
   uint32_t data_off;    // byte offset of slot 0
 };
 
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+__global__ void __launch_bounds__(staged_threads(kVPT), 1)
     row_staged_kernel(RowArgs a, const StagedCfg cfg, unsigned int* fault) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ float red[32];
-  constexpr int V = Elt<T>::kVec;
+  constexpr int V = Elt<T>::kVec, P = V / 2;
+  using S = Sets<kF>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = cfg.warps, m = cfg.m;
+  const int G = cfg.G, NG = cfg.warps / G, m = cfg.m;
+  const int grp = warp / G, wg = warp % G;
+  const int gl = wg * 32 + lane, GT = G * 32;  // thread within the group; group size
+  const bool leader = gl == 0;
   const int64_t per = (a.rows + gridDim.x - 1) / gridDim.x;
   const int64_t r0 = (int64_t)blockIdx.x * per;
   const int64_t rend = r0 + per < a.rows ? r0 + per : a.rows;
@@ -419,35 +567,40 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   const int nvec = (int)(a.cols / V);
   const uint32_t row_bytes = (uint32_t)nvec * 16u;
   const uint32_t base = smem_u32(smem_raw);
+  const uint32_t cache = base + cfg.cache_off;
+  const uint32_t set_bytes = (uint32_t)nvec * (uint32_t)V * 4u;
+  const GroupRed red{reinterpret_cast<float*>(smem_raw + cfg.red_off) + grp * 3 * kMaxG, G, wg, lane, 1 + grp};
 
-  // stage the broadcast vectors (gamma, beta, one-row scale/shift) once per CTA
+  // stage the broadcast operands once per CTA, converted to fp32 (scale as 1+scale)
   {
-    T* cache = reinterpret_cast<T*>(smem_raw + cfg.cache_off);
-    const int n = (int)a.cols;
-    const bool mod_b = a.scale != nullptr && a.mod_stride == 0;
-    const void* src[4] = {a.gamma, a.beta, mod_b ? a.scale : nullptr, mod_b ? a.shift : nullptr};
-    for (int v = 0; v < 4; ++v) {
-      if (!src[v]) continue;
-      const uint4* s4 = reinterpret_cast<const uint4*>(src[v]);
-      uint4* d4 = reinterpret_cast<uint4*>(cache + (size_t)v * n);
-      for (int k = threadIdx.x; k < nvec; k += blockDim.x) d4[k] = ld_bcast(s4 + k);
+    const void* src[5] = {a.gamma, a.beta, a.scale, a.shift, a.gate};
+    const int set_of[5] = {(kF & kFG) ? S::g : -1, (kF & kFB) ? S::b : -1, (kF & kFMod) ? S::c1 : -1,
+                           (kF & kFMod) ? S::sh : -1, (kF & kFGate) ? S::gate : -1};
+#pragma unroll
+    for (int o = 0; o < 5; ++o) {
+      if (set_of[o] < 0) continue;
+      const uint4* s4 = reinterpret_cast<const uint4*>(src[o]);
+      uint4* d4 = reinterpret_cast<uint4*>(smem_raw + cfg.cache_off + (size_t)set_of[o] * set_bytes);
+      const float add = o == 2 ? 1.f : 0.f;
+      for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+        float f[V];
+        Elt<T>::unpack(ld_bcast(s4 + k), f);
+#pragma unroll
+        for (int pl = 0; pl < V / 4; ++pl)
+          d4[pl * nvec + k] = make_uint4(__float_as_uint(f[4 * pl] + add), __float_as_uint(f[4 * pl + 1] + add),
+                                         __float_as_uint(f[4 * pl + 2] + add), __float_as_uint(f[4 * pl + 3] + add));
+      }
     }
-    if (mod_b) {  // the row math reads the cached copies from now on
-      a.scale = cache + 2 * (size_t)n;
-      a.shift = cache + 3 * (size_t)n;
-    }
-    if (a.gamma) a.gamma = cache;
-    if (a.beta) a.beta = cache + (size_t)n;
   }
-  if (threadIdx.x < W * m) mbar_init(base + 8u * threadIdx.x, 1);
+  if (threadIdx.x < NG * m) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
 
-  const uint32_t bar0 = base + 8u * (uint32_t)(warp * m);
-  const uint32_t slot0 = base + cfg.data_off + (uint32_t)(warp * m) * cfg.slot_bytes;
-  // unit k of this warp is row r0 + warp + k * W, in slot k % m, phase (k / m) & 1
+  const uint32_t bar0 = base + 8u * (uint32_t)(grp * m);
+  const uint32_t slot0 = base + cfg.data_off + (uint32_t)(grp * m) * cfg.slot_bytes;
+  // unit k of this group is row r0 + grp + k * NG, in slot k % m, phase (k / m) & 1
   auto issue = [&](int k) {
-    const int i = warp + k * W;
+    const int i = grp + k * NG;
     if (i >= units) return;
     const int64_t row = r0 + i;
     const uint32_t bar = bar0 + 8u * (uint32_t)(k % m), dst = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
@@ -460,39 +613,55 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       bulk_load(dst + row_bytes, reinterpret_cast<const T*>(a.res) + row * a.res_stride, row_bytes, bar);
     }
   };
-  if (lane == 0)
+  if (leader)
     for (int k = 0; k < m; ++k) issue(k);
   int k = 0;
-  for (; warp + k * W < units; ++k) {
+  for (; grp + k * NG < units; ++k) {
     const uint32_t bar = bar0 + 8u * (uint32_t)(k % m), sl = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
-    if (!mbar_wait(bar, (uint32_t)((k / m) & 1), fault)) break;
-    const int64_t row = r0 + warp + k * W;
+    // warp 0 of the group waits for the row; the others sleep at the group barrier
+    bool ok = true;
+    if (wg == 0) ok = mbar_wait(bar, (uint32_t)((k / m) & 1), fault);
+    if (!red.all(ok)) break;  // uniform across the group
+    const int64_t row = r0 + grp + k * NG;
     uint4 raw[kVPT];
+    {
 #pragma unroll
-    for (int v = 0; v < kVPT; ++v) {
-      const int idx = lane + 32 * v;
-      if (idx < nvec) {
-        if constexpr (kPro == kLoadX)
-          raw[v] = lds128(sl + idx * 16);
-        else if constexpr (kPro == kGeluX)
-          raw[v] = gelu_vec<T>(lds128(sl + idx * 16));
-        else  // h = residual + x * gate straight from the slot
-          raw[v] = resid_vec<T>(a, row, idx, lds128(sl + idx * 16), lds128(sl + row_bytes + idx * 16));
+      for (int v = 0; v < kVPT; ++v) {
+        const int idx = gl + GT * v;
+        if (idx < nvec) {
+          if constexpr (kPro == kLoadX) {
+            raw[v] = lds128(sl + idx * 16);
+          } else if constexpr (kPro == kGeluX) {
+            raw[v] = gelu_vec<T>(lds128(sl + idx * 16));
+          } else {  // h = residual + x * gate straight from the slot, rounded to T and stored
+            float2 x[P], r[P], g[P];
+            to_pairs<T>(lds128(sl + idx * 16), x);
+            to_pairs<T>(lds128(sl + row_bytes + idx * 16), r);
+            ld_set<V>(cache + S::gate * set_bytes, nvec, idx, g);
+#pragma unroll
+            for (int e = 0; e < P; ++e) x[e] = __ffma2_rn(x[e], g[e], r[e]);
+            raw[v] = from_pairs<T>(x);
+            st_global(reinterpret_cast<T*>(a.out_h) + row * a.h_stride + (int64_t)idx * V, raw[v]);
+          }
+        }
       }
     }
-    __syncwarp();
-    if (lane == 0) {
-      // the warp's shared-memory reads are done; order them before the copy
-      // engine overwrites the slot
+    // every warp of the group has read the slot before the leader refills it
+    if (G == 1)
+      __syncwarp();
+    else
+      red.sync();
+    if (leader) {
+      // order the group's shared-memory reads before the copy engine overwrites the slot
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(k + m);
     }
-    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, lane, red);
+    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, gl, cache, nvec, red);
   }
-  // error path only (a wait expired at unit k): the copies this warp issued
-  // for units k+1 .. k+m-1 must land before the CTA exits
-  if (lane == 0 && warp + k * W < units)
-    for (int j = k + 1; j < k + m && warp + j * W < units; ++j)
+  // error path only (a wait expired at unit k): the copies the leader issued
+  // for units k .. k+m-1 must land before the CTA exits
+  if (leader && grp + k * NG < units)
+    for (int j = k; j < k + m && grp + j * NG < units; ++j)
       mbar_wait(bar0 + 8u * (uint32_t)(j % m), (uint32_t)((j / m) & 1), fault);
 }
 
@@ -619,23 +788,38 @@ inline bool row_vec_ok(const RowArgs& a, int esize) {
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF>
 int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   auto kern = row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF>;
+  constexpr int V = Elt<T>::kVec;
   constexpr uint32_t kBudget = 216u * 1024u;
+  const int nvec = (int)(a.cols / V);
   const uint32_t row_bytes = (uint32_t)(a.cols * sizeof(T)) * (kPro == kResidGate ? 2u : 1u);
   StagedCfg cfg{};
   cfg.slot_bytes = (row_bytes + 127u) & ~127u;
-  const uint32_t cache_bytes = (uint32_t)(4 * a.cols * sizeof(T) + 127) & ~127u;
-  const uint32_t avail = kBudget - cache_bytes - 1024u;
-  cfg.warps = kMaxWarps;
-  cfg.m = (int)(avail / ((uint32_t)cfg.warps * cfg.slot_bytes));
+  // one warp per row, except two-input rows (residual + x), whose row groups
+  // of G warps hold at most kVPT vectors per thread; warps per CTA by the
+  // register budget (30 for G = 2: named barriers 1..15 name the groups)
+  cfg.G = kPro != kResidGate || nvec <= 32 * kVPT ? 1 : (nvec <= 64 * kVPT ? 2 : 4);
+  if (cfg.G * 32 * kVPT < nvec) return fail(JO_ERR_SHAPE, "row kernel: row group too small");
+  cfg.warps = staged_threads(kVPT) / 32;
+  if (cfg.G == 2 && cfg.warps > 30) cfg.warps = 30;
+  const uint32_t cache_bytes = (uint32_t)(Sets<kF>::n * 4 * a.cols + 127) & ~127u;
+  if (cache_bytes + 2048u >= kBudget) return fail(JO_ERR_SHAPE, "row kernel: rows too large to stage");
+  const uint32_t avail = kBudget - cache_bytes - 2048u;
+  // ~6 KB in flight per group is enough to cover the load latency: one slot
+  // for 3072-wide bf16 rows, up to three for short rows
+  int ng = cfg.warps / cfg.G;
+  cfg.m = (int)((6144u + cfg.slot_bytes - 1) / cfg.slot_bytes);
   if (cfg.m > 3) cfg.m = 3;
-  if (cfg.m < 1) {
-    cfg.m = 1;
-    cfg.warps = (int)(avail / cfg.slot_bytes);
+  while (cfg.m > 1 && (uint32_t)(ng * cfg.m) * cfg.slot_bytes > avail) --cfg.m;
+  if ((uint32_t)ng * cfg.slot_bytes > avail) {  // fewer groups, one slot each
+    ng = (int)(avail / cfg.slot_bytes);
+    cfg.warps = ng * cfg.G;
   }
-  if (cfg.warps < 4) return fail(JO_ERR_SHAPE, "row kernel: rows too large to stage");
-  cfg.cache_off = (uint32_t)((8 * cfg.warps * cfg.m + 127) & ~127);
+  ng = cfg.warps / cfg.G;
+  if (ng < 1) return fail(JO_ERR_SHAPE, "row kernel: rows too large to stage");
+  cfg.red_off = (uint32_t)((8 * ng * cfg.m + 15) & ~15);
+  cfg.cache_off = (cfg.red_off + (uint32_t)(ng * 3 * kMaxG * 4) + 127u) & ~127u;
   cfg.data_off = cfg.cache_off + cache_bytes;
-  const size_t smem = cfg.data_off + (size_t)cfg.warps * cfg.m * cfg.slot_bytes;
+  const size_t smem = cfg.data_off + (size_t)ng * cfg.m * cfg.slot_bytes;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
@@ -643,34 +827,43 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
     attr = true;
   }
   int64_t grid = di->sm_count;
-  const int64_t min_rows = 2 * cfg.warps;  // at least two rows per warp before adding CTAs
+  const int64_t min_rows = 2 * ng;  // at least two rows per group before adding CTAs
   if (grid * min_rows > a.rows) grid = cdiv(a.rows, min_rows);
   if (grid < 1) grid = 1;
   kern<<<(unsigned)grid, cfg.warps * 32, smem, st>>>(a, cfg, di->fault);
   return after_launch("row_staged_kernel");
 }
 
+// The staged path takes broadcast (one-row) modulation and gate operands only;
+// per-row operands go to the block path.
+inline bool staged_operands_ok(const RowArgs& a, int pro) {
+  if (a.scale != nullptr && a.mod_stride != 0) return false;
+  if (pro == kResidGate && a.gate_stride != 0) return false;
+  return true;
+}
+
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi>
 int launch_staged(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
+  constexpr int kG = kPro == kResidGate ? kFGate : 0;
   const bool g = a.gamma != nullptr, b = a.beta != nullptr, mod = a.scale != nullptr;
   if constexpr (kNorm == kNoNorm) {
-    return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, 0>(a, st, di);
+    return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG>(a, st, di);
   } else if constexpr (kNorm == kRms) {  // beta is a LayerNorm-only operand
-    if (mod) return g ? launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG | kFMod>(a, st, di)
-                      : launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFMod>(a, st, di);
-    return g ? launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG>(a, st, di)
-             : launch_staged_f<T, kVPT, kNorm, kPro, kEpi, 0>(a, st, di);
+    if (mod) return g ? launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG | kFMod>(a, st, di)
+                      : launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFMod>(a, st, di);
+    return g ? launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG>(a, st, di)
+             : launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG>(a, st, di);
   } else {
     if (mod) {
-      if (g && b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG | kFB | kFMod>(a, st, di);
-      if (g) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG | kFMod>(a, st, di);
-      if (b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFB | kFMod>(a, st, di);
-      return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFMod>(a, st, di);
+      if (g && b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG | kFB | kFMod>(a, st, di);
+      if (g) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG | kFMod>(a, st, di);
+      if (b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFB | kFMod>(a, st, di);
+      return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFMod>(a, st, di);
     }
-    if (g && b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG | kFB>(a, st, di);
-    if (g) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFG>(a, st, di);
-    if (b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kFB>(a, st, di);
-    return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, 0>(a, st, di);
+    if (g && b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG | kFB>(a, st, di);
+    if (g) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFG>(a, st, di);
+    if (b) return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG | kFB>(a, st, di);
+    return launch_staged_f<T, kVPT, kNorm, kPro, kEpi, kG>(a, st, di);
   }
 }
 
@@ -688,12 +881,18 @@ int launch_rows_t(const RowArgs& a, cudaStream_t st) {
   if (int s = device_info(&di)) return s;
   if (row_vec_ok(a, sizeof(T))) {
     const int nvec = (int)(a.cols / V);
-    if (nvec <= 32 * 16) {
-      const int per = (nvec + 31) / 32;
+    if (nvec <= 32 * 16 && staged_operands_ok(a, kPro)) {
 #define JO_STAGED(VPT) return launch_staged<T, VPT, kNorm, kPro, kEpi>(a, st, di)
-      if (per <= 4) JO_STAGED(4);
-      if (per <= 8) JO_STAGED(8);
-      if (per <= 12) JO_STAGED(12);
+      // vectors per thread: one warp per row, or (residual + x rows) the
+      // smallest row group G in {1, 2, 4} with at most 4 vectors per thread
+      const int G = kPro != kResidGate || nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
+      const int vpt = (nvec + 32 * G - 1) / (32 * G);
+      if (vpt <= 2) JO_STAGED(2);
+      if (vpt <= 3) JO_STAGED(3);
+      if (vpt <= 4) JO_STAGED(4);
+      if (vpt <= 6) JO_STAGED(6);
+      if (vpt <= 8) JO_STAGED(8);
+      if (vpt <= 12) JO_STAGED(12);
       JO_STAGED(16);
 #undef JO_STAGED
     }

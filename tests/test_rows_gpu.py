@@ -13,7 +13,8 @@ from oracle import ops
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(3600, 3072), (1, 3072), (0, 3072), (37, 136), (5, 12288), (9, 100), (4, 24576), (3, 40000)]
+SHAPES = [(3600, 3072), (1, 3072), (0, 3072), (37, 136), (5, 12288), (9, 100), (4, 24576), (3, 40000),
+          (11, 2048), (13, 1536), (150, 1024)]  # row groups of 1, 2 and 4 warps
 DTYPES = [torch.bfloat16, torch.float16, torch.float32]
 
 
@@ -129,7 +130,8 @@ def quant_inputs(M, N, dt, seed):
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("shape", [(10800, 3072), (67, 4096), (1, 16), (0, 3072), (9, 100), (5, 12288), (6, 24)])
+@pytest.mark.parametrize("shape", [(10800, 3072), (67, 4096), (1, 16), (0, 3072), (9, 100), (5, 12288), (6, 24),
+                                   (19, 2048), (7, 1040)])
 def test_per_token_quant_bit_exact(jo, dev, dt, shape):
     M, N = shape
     x = quant_inputs(M, N, dt, 40)
