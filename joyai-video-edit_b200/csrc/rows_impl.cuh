@@ -375,10 +375,12 @@ struct GroupRed {
 
 // Row math of the staged path, f32x2 throughout.  Same operation order as
 // row_math (LayerNorm ((x-mean)*rstd*g + b)*(1+sc)+sh, RMS (x*rstd*g)*(1+sc)+sh;
-// two-pass mean/variance; quant on the T-rounded y).
+// two-pass mean/variance; quant on the T-rounded y).  The statistics use the
+// reciprocal of the row length and the hardware rsqrt, as the reference kernel
+// does (fused_norm_scale_shift.cu:136,157): both move rstd by a few fp32 ulps.
 template <typename T, int kVPT, int kNorm, int kEpi, int kF>
 __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT], int lane,
-                                          uint32_t cache, int nvec, const GroupRed& red) {
+                                          uint32_t cache, int nvec, float inv_n, const GroupRed& red) {
   const int GT = red.G * 32;  // threads of the row group; this thread's vectors: lane + GT * i
   constexpr int V = Elt<T>::kVec, P = V / 2;
   constexpr bool k16 = V == 8;
@@ -399,7 +401,7 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
           s1 = __fadd2_rn(s1, p[e + 1]);
         }
       }
-    mean = __fdiv_rn(red.sum((s0.x + s1.x) + (s0.y + s1.y), 0), (float)a.cols);
+    mean = red.sum((s0.x + s1.x) + (s0.y + s1.y), 0) * inv_n;
     const float2 nm = f2(-mean);
     float2 q0 = f2(0.f), q1 = f2(0.f);
 #pragma unroll
@@ -414,7 +416,7 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
           q1 = __ffma2_rn(d1, d1, q1);
         }
       }
-    rstd = rsqrt_ieee(__fdiv_rn(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), (float)a.cols) + a.eps);
+    rstd = rsqrtf(fmaf(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), inv_n, a.eps));
   } else if constexpr (kNorm == kRms) {
     float2 q0 = f2(0.f), q1 = f2(0.f);
 #pragma unroll
@@ -428,7 +430,7 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
           q1 = __ffma2_rn(p[e + 1], p[e + 1], q1);
         }
       }
-    rstd = rsqrt_ieee(__fdiv_rn(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), (float)a.cols) + a.eps);
+    rstd = rsqrtf(fmaf(red.sum((q0.x + q1.x) + (q0.y + q1.y), 1), inv_n, a.eps));
   }
   const float2 nm2 = f2(-mean), r2 = f2(rstd);
   uint32_t amax16 = 0u;  // 16-bit types: packed |y| maximum
@@ -569,6 +571,7 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t cache = base + cfg.cache_off;
   const uint32_t set_bytes = (uint32_t)nvec * (uint32_t)V * 4u;
+  const float inv_n = 1.0f / (float)a.cols;
   const GroupRed red{reinterpret_cast<float*>(smem_raw + cfg.red_off) + grp * 3 * kMaxG, G, wg, lane, 1 + grp};
 
   // stage the broadcast operands once per CTA, converted to fp32 (scale as 1+scale)
@@ -656,7 +659,7 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(k + m);
     }
-    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, gl, cache, nvec, red);
+    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, gl, cache, nvec, inv_n, red);
   }
   // error path only (a wait expired at unit k): the copies the leader issued
   // for units k .. k+m-1 must land before the CTA exits
@@ -808,6 +811,9 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   // for 3072-wide bf16 rows, up to three for short rows
   int ng = cfg.warps / cfg.G;
   cfg.m = (int)((6144u + cfg.slot_bytes - 1) / cfg.slot_bytes);
+  // a group with only 2-3 rows in all keeps all of them in flight from the start
+  const int64_t group_rows = cdiv(cdiv(a.rows, (int64_t)di->sm_count), (int64_t)ng);
+  if (group_rows <= 3 && cfg.m < group_rows) cfg.m = (int)group_rows;
   if (cfg.m > 3) cfg.m = 3;
   while (cfg.m > 1 && (uint32_t)(ng * cfg.m) * cfg.slot_bytes > avail) --cfg.m;
   if ((uint32_t)ng * cfg.slot_bytes > avail) {  // fewer groups, one slot each
