@@ -7,6 +7,9 @@
 // (:1015-1159).  This kernel is written directly against the sm_100a
 // instructions; every CTA loads its own operand tiles (no cross-CTA broadcast):
 //
+//   * CTA pairs (fp8_gemm_pair_kernel, below) for M > 128: 256 x 256 tiles per
+//     pair of SMs with tcgen05.mma.cta_group::2; the single-CTA kernel here
+//     takes M <= 128;
 //   * persistent: one CTA per SM walks output tiles of 128 x 256;
 //   * warp 0, one lane: TMA producer.  A tile 128 x 128 B and B tile 256 x 128 B
 //     per k-block (128-byte swizzle, K-major), kStages-deep mbarrier ring;
@@ -308,6 +311,279 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel
+// Two CTAs of a (2,1,1) cluster share one 256 x 256 output tile through
+// tcgen05.mma.cta_group::2 (M = 256): CTA rank r loads A rows [128r, 128r+128)
+// and B columns [128r, 128r+128) of the tile (32 KB per k-block instead of the
+// 48 KB a single CTA needs for 128 x 256), the leader CTA (rank 0) issues the
+// MMAs, and each CTA's tensor memory receives its 128 rows x 256 columns.
+//   * both producers wait on their own `empty` barrier, then load with the
+//     .cta_group::2 TMA form, completing bytes on the LEADER's `full` barrier;
+//     the leader's producer alone expects the pair's 64 KB per stage;
+//   * the leader's MMA thread releases a stage / publishes an accumulator with
+//     one tcgen05.commit per CTA (its own barrier and the peer's, by cluster
+//     address);
+//   * the epilogue threads of both CTAs arrive on the leader's `tmem empty`
+//     barrier (256 arrivals), the peer's remotely.
+// Every load is a plain (non-broadcast) TMA load of this GPU's memory.
+constexpr int kP_BM = 128;                  // A rows per CTA (pair tile: 256)
+constexpr int kP_BN = 256;                  // pair tile N (128 B columns per CTA)
+constexpr int kP_Stages = 6;
+constexpr int kP_StageA = kP_BM * kBK;      // 16 KB
+constexpr int kP_StageB = (kP_BN / 2) * kBK;  // 16 KB
+constexpr int kP_SmemBytes = kP_Stages * (kP_StageA + kP_StageB) + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t kIdescPair = (1u << 4)                              // D format f32
+                                | ((uint32_t)(kP_BN >> 3) << 17)        // N >> 3
+                                | ((uint32_t)((2 * kP_BM) >> 4) << 24);  // M >> 4 (M = 256)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// TMA tile load into this CTA's shared memory, bytes completed on `bar`, which
+// may be the peer CTA's barrier (cluster address)
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` (cluster address) once this thread's prior pair MMAs complete
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+constexpr int kP_EpiWarps = 8;                     // 2 per TMEM lane quadrant, 128 columns each
+constexpr int kP_Threads = 64 + 32 * kP_EpiWarps;  // producer warp, MMA warp, epilogue warps
+
+template <typename OutT, bool kBias>
+__global__ void __launch_bounds__(kP_Threads, 1)
+    fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const GemmArgs args) {
+  unsigned int* const fault = args.fault;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t base = (raw_base + 1023u) & ~1023u;  // identical offsets in both CTAs
+  uint8_t* gbase = smem_raw + (base - raw_base);
+  const uint32_t sA = base;                           // kP_Stages x 16 KB
+  const uint32_t sB = base + kP_Stages * kP_StageA;   // kP_Stages x 16 KB
+  const uint32_t bars = sB + kP_Stages * kP_StageB;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (kP_Stages + s); };
+  auto tfull_bar = [&](int b) { return bars + 8u * (2 * kP_Stages + b); };
+  auto tempty_bar = [&](int b) { return bars + 8u * (2 * kP_Stages + 2 + b); };
+  const uint32_t done_bar = bars + 8u * (2 * kP_Stages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * kP_Stages + 5));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cluster = (int)(blockIdx.x >> 1), nclusters = (int)(gridDim.x >> 1);
+  const int num_tiles = args.tiles_m * args.tiles_n;  // pair tiles of 256 x 256
+  const int kblocks = (args.k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kP_Stages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 2 * kP_EpiWarps * 32);  // the epilogue threads of both CTAs
+    }
+    mbar_init(done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {  // same warp in both CTAs: the pair allocation is collective
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_phase[kP_Stages];
+      bool issued[kP_Stages];
+      for (int s = 0; s < kP_Stages; ++s) issued[s] = false;
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, fault)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = cluster_addr(full_bar(stage), 0);
+          if (leader) mbar_expect_tx(full_bar(stage), 2 * (kP_StageA + kP_StageB));
+          tma_load_2d_pair(sA + stage * kP_StageA, &map_a, kb * kBK, tm * (2 * kP_BM) + (int)rank * kP_BM, fb);
+          tma_load_2d_pair(sB + stage * kP_StageB, &map_b, kb * kBK, tn * kP_BN + (int)rank * (kP_BN / 2), fb);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == kP_Stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // drain (leader): the pair's copies into every issued stage must have landed
+      // (the leader's full barriers count both CTAs' bytes); the peer is held by
+      // the final cluster barrier until then
+      if (leader)
+        for (int s = 0; s < kP_Stages; ++s)
+          if (issued[s]) mbar_wait(full_bar(s), issued_phase[s], fault);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, fault)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kP_BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, fault)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * kP_StageA, b0 = sB + stage * kP_StageB;
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk)
+            tc_mma_pair(d_tmem, sw128_desc(a0 + kk * kUmmaK), sw128_desc(b0 + kk * kUmmaK), kIdescPair,
+                        (kb | kk) != 0);
+          // the stage is reusable in both CTAs once these MMAs have read it
+          tc_commit_pair(empty_bar(stage));
+          tc_commit_pair(cluster_addr(empty_bar(stage), 1));
+          if (++stage == kP_Stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit_pair(tfull_bar(acc));  // accumulator complete, in both CTAs
+        tc_commit_pair(cluster_addr(tfull_bar(acc), 1));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // TMEM is freed below and the peer's shared memory is read by these
+      // MMAs: wait until every one of them has retired
+      tc_commit_pair(done_bar);
+      mbar_wait(done_bar, 0, fault);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..9 of both CTAs; warp w reads TMEM lanes
+    // 32*(w%4) .. +31 (the lane quadrant its warp slot may access) and column half
+    // (w-2)/4 of the accumulator
+    const int q = warp & 3, half = (warp - 2) >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    OutT* D = reinterpret_cast<OutT*>(args.d);
+    const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
+    for (int tile = cluster; tile < num_tiles; tile += nclusters) {
+      const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
+      tc_fence_after();
+      const int row = tm * (2 * kP_BM) + (int)rank * kP_BM + q * 32 + lane;
+      const bool row_ok = row < args.m;
+      const float s_a = row_ok ? __ldg(args.sa + row) : 0.f;
+      OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kP_BN);
+#pragma unroll 1
+      for (int c = half * (kP_BN / 64); c < (half + 1) * (kP_BN / 64); ++c) {
+        const int n0 = tn * kP_BN + c * 32;
+        uint32_t r[32];
+        tmem_ld32(t_row + (uint32_t)(c * 32), r);
+        if (n0 >= args.n) continue;  // whole chunk past N (uniform across the warp)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+          const int ng = n0 + g * 8;
+          if (ng >= args.n) break;
+          const float4 sb0 = __ldg(reinterpret_cast<const float4*>(args.sb + ng));
+          const float4 sb1 = __ldg(reinterpret_cast<const float4*>(args.sb + ng + 4));
+          const float sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
+          float bv[8];
+          if constexpr (kBias) {
+            float t[8];
+            Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(bias + ng)), t);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) bv[e] = t[e];
+          }
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float t = __uint_as_float(r[g * 8 + e]) * sb[e];
+            o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
+          }
+          if (row_ok) {
+            uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
+                                 pack2<OutT>(o[6], o[7]));
+            *reinterpret_cast<uint4*>(drow + ng) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      if (leader)
+        mbar_arrive(tempty_bar(acc));
+      else
+        mbar_arrive_cluster(cluster_addr(tempty_bar(acc), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+  __syncthreads();
+  // neither CTA leaves while the other may still signal its barriers or have
+  // its shared memory read by the pair's MMAs
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 // ------------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -353,6 +629,48 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
   return after_launch("fp8_gemm_kernel");
 }
 
+// CTA-pair launch: clusters of (2,1,1), as many as can be resident at once.
+template <typename OutT, bool kBias>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st) {
+  auto kern = fp8_gemm_pair_kernel<OutT, kBias>;
+  static int max_clusters = 0;
+  if (!max_clusters) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kP_SmemBytes) != cudaSuccess)
+      return fail(JO_ERR_CUDA, "fp8_scaled_mm: cannot reserve %d bytes of shared memory", kP_SmemBytes);
+    cudaLaunchConfig_t qc = {};
+    qc.gridDim = dim3(2, 1, 1);
+    qc.blockDim = dim3(kP_Threads, 1, 1);
+    qc.dynamicSmemBytes = kP_SmemBytes;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &qc) != cudaSuccess || n < 1)
+      return fail(JO_ERR_CUDA, "fp8_scaled_mm: no resident CTA pair");
+    max_clusters = n;
+  }
+  const int tiles = a.tiles_m * a.tiles_n;
+  const int clusters = tiles < max_clusters ? tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kP_Threads, 1, 1);
+  cfg.dynamicSmemBytes = kP_SmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, a) != cudaSuccess) return fail(JO_ERR_CUDA, "fp8_scaled_mm: pair launch failed");
+  return after_launch("fp8_gemm_pair_kernel");
+}
+
 }  // namespace
 }  // namespace jo
 
@@ -377,9 +695,11 @@ int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const voi
   if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: size too large", op);
   if (!aligned16(d) || !aligned16(a) || !aligned16(b) || !aligned16(scale_b) || (bias && !aligned16(bias)))
     return fail(JO_ERR_ALIGN, "%s: D, A, B, scale_b and bias must be 16-byte aligned", op);
+  // CTA pairs (256 x 256 tiles) unless A is a single 128-row tile
+  const bool pair = m > kBM;
   CUtensorMap ma, mb;
-  if (int s = make_map(&ma, a, m, k, lda, kBM)) return s;
-  if (int s = make_map(&mb, b, n, k, ldb, kBN)) return s;
+  if (int s = make_map(&ma, a, m, k, lda, pair ? kP_BM : kBM)) return s;
+  if (int s = make_map(&mb, b, n, k, ldb, pair ? kP_BN / 2 : kBN)) return s;
   GemmArgs g{};
   g.d = d;
   g.ldd = ldd;
@@ -389,11 +709,16 @@ int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const voi
   g.m = (int)m;
   g.n = (int)n;
   g.k = (int)k;
-  g.tiles_m = (int)cdiv(m, kBM);
-  g.tiles_n = (int)cdiv(n, kBN);
+  g.tiles_m = (int)cdiv(m, pair ? 2 * kP_BM : kBM);
+  g.tiles_n = (int)cdiv(n, pair ? kP_BN : kBN);
   g.fault = di->fault;
   if ((int64_t)g.tiles_m * g.tiles_n > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many tiles", op);
   cudaStream_t st = (cudaStream_t)stream;
+  if (pair) {
+    if (out_dtype == JO_BF16)
+      return bias ? launch_gemm_pair<__nv_bfloat16, true>(ma, mb, g, st) : launch_gemm_pair<__nv_bfloat16, false>(ma, mb, g, st);
+    return bias ? launch_gemm_pair<__half, true>(ma, mb, g, st) : launch_gemm_pair<__half, false>(ma, mb, g, st);
+  }
   if (out_dtype == JO_BF16)
     return bias ? launch_gemm<__nv_bfloat16, true>(ma, mb, g, st, di) : launch_gemm<__nv_bfloat16, false>(ma, mb, g, st, di);
   return bias ? launch_gemm<__half, true>(ma, mb, g, st, di) : launch_gemm<__half, false>(ma, mb, g, st, di);
