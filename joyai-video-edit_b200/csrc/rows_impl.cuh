@@ -574,27 +574,6 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   const float inv_n = 1.0f / (float)a.cols;
   const GroupRed red{reinterpret_cast<float*>(smem_raw + cfg.red_off) + grp * 3 * kMaxG, G, wg, lane, 1 + grp};
 
-  // stage the broadcast operands once per CTA, converted to fp32 (scale as 1+scale)
-  {
-    const void* src[5] = {a.gamma, a.beta, a.scale, a.shift, a.gate};
-    const int set_of[5] = {(kF & kFG) ? S::g : -1, (kF & kFB) ? S::b : -1, (kF & kFMod) ? S::c1 : -1,
-                           (kF & kFMod) ? S::sh : -1, (kF & kFGate) ? S::gate : -1};
-#pragma unroll
-    for (int o = 0; o < 5; ++o) {
-      if (set_of[o] < 0) continue;
-      const uint4* s4 = reinterpret_cast<const uint4*>(src[o]);
-      uint4* d4 = reinterpret_cast<uint4*>(smem_raw + cfg.cache_off + (size_t)set_of[o] * set_bytes);
-      const float add = o == 2 ? 1.f : 0.f;
-      for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
-        float f[V];
-        Elt<T>::unpack(ld_bcast(s4 + k), f);
-#pragma unroll
-        for (int pl = 0; pl < V / 4; ++pl)
-          d4[pl * nvec + k] = make_uint4(__float_as_uint(f[4 * pl] + add), __float_as_uint(f[4 * pl + 1] + add),
-                                         __float_as_uint(f[4 * pl + 2] + add), __float_as_uint(f[4 * pl + 3] + add));
-      }
-    }
-  }
   if (threadIdx.x < NG * m) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
@@ -618,6 +597,29 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   };
   if (leader)
     for (int k = 0; k < m; ++k) issue(k);
+  // stage the broadcast operands once per CTA, converted to fp32 (scale as 1+scale),
+  // while the first rows are in flight
+  {
+    const void* src[5] = {a.gamma, a.beta, a.scale, a.shift, a.gate};
+    const int set_of[5] = {(kF & kFG) ? S::g : -1, (kF & kFB) ? S::b : -1, (kF & kFMod) ? S::c1 : -1,
+                           (kF & kFMod) ? S::sh : -1, (kF & kFGate) ? S::gate : -1};
+#pragma unroll
+    for (int o = 0; o < 5; ++o) {
+      if (set_of[o] < 0) continue;
+      const uint4* s4 = reinterpret_cast<const uint4*>(src[o]);
+      uint4* d4 = reinterpret_cast<uint4*>(smem_raw + cfg.cache_off + (size_t)set_of[o] * set_bytes);
+      const float add = o == 2 ? 1.f : 0.f;
+      for (int k = threadIdx.x; k < nvec; k += blockDim.x) {
+        float f[V];
+        Elt<T>::unpack(ld_bcast(s4 + k), f);
+#pragma unroll
+        for (int pl = 0; pl < V / 4; ++pl)
+          d4[pl * nvec + k] = make_uint4(__float_as_uint(f[4 * pl] + add), __float_as_uint(f[4 * pl + 1] + add),
+                                         __float_as_uint(f[4 * pl + 2] + add), __float_as_uint(f[4 * pl + 3] + add));
+      }
+    }
+  }
+  __syncthreads();
   int k = 0;
   for (; grp + k * NG < units; ++k) {
     const uint32_t bar = bar0 + 8u * (uint32_t)(k % m), sl = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
