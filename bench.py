@@ -8,7 +8,8 @@ on the (t, h, w) grid with a random chunk start t0 in [0, 64).  One step = one
 pass of the op over one chunk.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload qkv_pack|rmsnorm|ln_mod|gated_ln|gelu|silu_mul|quant|rmsnorm_quant]
+                    [--workload qkv_pack|rmsnorm|ln_mod|gated_ln|gelu|silu_mul|quant|rmsnorm_quant|
+                                gemm_qkv|gemm_up|temb|chain]
 
 N > 1 runs under torchrun, one process per GPU; every rank processes its own
 chunk (independent token partitions: weak scaling, no collective on the data
@@ -298,6 +299,57 @@ class Gemm(Workload):
         return ((x["aq"].float() * x["sa"]) @ (x["bq"] * x["sb"])).to(BF)
 
 
+class Temb(Workload):
+    """Timestep conditioning MLP at the model's shape (batch 1): sinusoid(256) -> linear_1
+    (3072x256) -> SiLU -> linear_2 (3072x3072) -> SiLU -> time_proj (18432x3072); bound by
+    the 133 MB weight read (dit.py:574-579, 605-620, §8f rank 4)."""
+
+    name = "temb"
+    desc = "timestep MLP: sinusoid(256) -> 3072 -> 3072 -> 18432, batch 1 (dit.py:574-620)"
+    B, F_, D, P_ = 1, 256, 3072, 6 * 3072
+
+    def __init__(self):
+        self.shape = {"batch": self.B, "freq_dim": self.F_, "dim": self.D, "proj_dim": self.P_,
+                      "weights": "bf16 N(0, 1/fan_in), biases N(0, 0.1)"}
+
+    def algo_bytes(self):
+        w = self.D * self.F_ + self.D * self.D + self.P_ * self.D
+        return 2 * (w + 2 * self.D + self.P_) + 4 * self.B + 2 * self.B * self.P_
+
+    def _inputs(self, seed, dev):
+        g = torch.Generator().manual_seed(seed)
+        w = lambda n, k: (torch.randn(n, k, generator=g) / k ** 0.5).to(BF).to(dev)
+        b = lambda n: (0.1 * torch.randn(n, generator=g)).to(BF).to(dev)
+        t = (torch.rand(self.B, generator=g) * 1000.0).to(dev)
+        return dict(t=t, w1=w(self.D, self.F_), b1=b(self.D), w2=w(self.D, self.D), b2=b(self.D),
+                    w3=w(self.P_, self.D), b3=b(self.P_))
+
+    def make(self, dev, seed):
+        import joyomni_ops as jo
+
+        x = self._inputs(seed, dev)
+        st = dict(x=x, jo=jo)
+        vec, _ = self.step(st)
+        return dict(st, inputs={"t": x["t"]}, outputs={"vec": vec})
+
+    def step(self, st):
+        x = st["x"]
+        return st["jo"].timestep_mlp(x["t"], x["w1"], x["b1"], x["w2"], x["b2"], x["w3"], x["b3"])
+
+    def e2e_step(self, st, host_in, host_out):
+        st["x"]["t"].copy_(host_in["t"], non_blocking=True)
+        vec, _ = self.step(st)
+        host_out["vec"].copy_(vec, non_blocking=True)
+
+    def make_cpu(self, seed):
+        return self._inputs(seed, "cpu")
+
+    def cpu_step(self, x):
+        from oracle import ops
+
+        return ops.timestep_mlp(x["t"], x["w1"], x["b1"], x["w2"], x["b2"], x["w3"], x["b3"])
+
+
 class Chain(Workload):
     """One MMDoubleStreamBlock forward for one streaming chunk:
     10800 video + 512 text tokens, hidden 3072, 24 x 128 heads, FFN 12288, KV cache of
@@ -391,6 +443,7 @@ def workloads():
         "gemm_qkv": Gemm("gemm_qkv", 10800, 9216, 3072, "FP8 GEMM QKV projection [10800,3072]x[3072,9216] (configs[3])"),
         "gemm_up": Gemm("gemm_up", 10800, 12288, 3072, "FP8 GEMM MLP-up [10800,3072]x[3072,12288] (configs[3])"),
         "chain": Chain(),
+        "temb": Temb(),
     }
 
 

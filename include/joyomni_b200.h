@@ -212,6 +212,21 @@ JO_API int jo_timestep_embedding(float* out, const float* t, int64_t batch, int6
                           int flip_sin_to_cos, float downscale_freq_shift, float scale,
                           float max_period, void* stream);
 
+/* Timestep conditioning MLP, the WanTimeTextImageEmbedding timestep branch
+ * (deploy/xvideo/models/dit/dit.py:574-579, 605-620; replaces Timesteps +
+ * TimestepEmbedding + act_fn + time_proj, four modules and seven kernels):
+ *   e = bf16(sinusoid(t)) [B, freq_dim] (flip_sin_to_cos, shift 0, max_period),
+ *   s1 = bf16(silu(bf16(e @ w1^T + b1))), s2 = bf16(silu(bf16(s1 @ w2^T + b2))),
+ *   vec = bf16(s2 @ w3^T + b3) [B, proj_dim].
+ * w1 bf16 [dim, freq_dim], w2 [dim, dim], w3 [proj_dim, dim] row-major; biases
+ * bf16 or NULL; t fp32 [B].  freq_dim, dim <= 4096, multiples of 8.
+ * scratch: caller-owned device memory of >= 4 * B * dim bytes (16-byte aligned)
+ * that receives s1 then s2 (bf16 [B, dim] each). */
+JO_API int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void* w1, const void* b1,
+                           int64_t freq_dim, int64_t dim, const void* w2, const void* b2, const void* w3,
+                           const void* b3, int64_t proj_dim, void* scratch, int64_t scratch_bytes,
+                           float max_period, void* stream);
+
 /* RMSNorm -> per-token FP8 quant, one pass: y = dtype(rmsnorm(x)*w) is rounded
  * to dtype in registers, then quantised with the jo_per_token_quant_fp8
  * semantics.  Oracle: quant(_torch_rmsnorm(x, w, eps)). */

@@ -543,6 +543,44 @@ torch::Tensor timestep_embedding(const torch::Tensor& t, int64_t dim, bool flip_
   return out;
 }
 
+// Returns (vec [B, proj_dim], s2 [B, dim]): s2 = silu(temb) is the time_proj input
+// (the second intermediate, kept for callers that reuse it).
+std::tuple<torch::Tensor, torch::Tensor> timestep_mlp(const torch::Tensor& t, const torch::Tensor& w1,
+                                                      const c10::optional<torch::Tensor>& b1,
+                                                      const torch::Tensor& w2,
+                                                      const c10::optional<torch::Tensor>& b2,
+                                                      const torch::Tensor& w3,
+                                                      const c10::optional<torch::Tensor>& b3, double max_period) {
+  JO_CHECK_CUDA(t);
+  TORCH_CHECK(t.dim() == 1, "timesteps must be 1D");
+  for (const torch::Tensor* w : {&w1, &w2, &w3})
+    TORCH_CHECK(w->dim() == 2 && w->is_contiguous() && w->scalar_type() == torch::kBFloat16 &&
+                    w->device() == t.device(),
+                "weights must be contiguous bf16 [out, in] on the timesteps' device");
+  const int64_t dim = w1.size(0), freq = w1.size(1), proj = w3.size(0);
+  TORCH_CHECK(w2.size(0) == dim && w2.size(1) == dim && w3.size(1) == dim, "weight shapes do not chain");
+  auto bias_ptr = [&](const c10::optional<torch::Tensor>& b, int64_t n) -> const void* {
+    if (!b.has_value()) return nullptr;
+    TORCH_CHECK(b->dim() == 1 && b->numel() == n && b->is_contiguous() && b->scalar_type() == torch::kBFloat16 &&
+                    b->device() == t.device(),
+                "bias must be contiguous bf16 [out] on the timesteps' device");
+    return b->data_ptr();
+  };
+  const void* pb1 = bias_ptr(b1, dim);
+  const void* pb2 = bias_ptr(b2, dim);
+  const void* pb3 = bias_ptr(b3, proj);
+  auto tf = t.to(torch::kFloat32).contiguous();
+  const c10::cuda::CUDAGuard guard(t.device());
+  const int64_t B = t.size(0);
+  auto vec = torch::empty({B, proj}, w1.options());
+  auto scratch = torch::empty({2, B, dim}, w1.options());  // s1, s2
+  jo_check(jo_timestep_mlp(vec.data_ptr(), tf.data_ptr<float>(), B, w1.data_ptr(), pb1, freq, dim, w2.data_ptr(),
+                           pb2, w3.data_ptr(), pb3, proj, scratch.data_ptr(), scratch.numel() * 2,
+                           (float)max_period, stream_of(t)),
+           "timestep_mlp");
+  return std::make_tuple(vec, scratch[1]);
+}
+
 std::tuple<torch::Tensor, torch::Tensor> rmsnorm_quant_fp8(const torch::Tensor& x, const torch::Tensor& weight,
                                                            double eps) {
   JO_CHECK_CUDA(x);
@@ -621,6 +659,9 @@ TORCH_LIBRARY(joyomni_ops, m) {
   m.def(
       "timestep_embedding(Tensor t, int dim, bool flip_sin_to_cos, float downscale_freq_shift, "
       "float scale, float max_period) -> Tensor");
+  m.def(
+      "timestep_mlp(Tensor t, Tensor w1, Tensor? b1, Tensor w2, Tensor? b2, Tensor w3, Tensor? b3, "
+      "float max_period) -> (Tensor, Tensor)");
   m.def("rmsnorm_quant_fp8(Tensor x, Tensor weight, float eps) -> (Tensor, Tensor)");
   m.def(
       "norm_scale_shift_quant_fp8(Tensor x, Tensor? gamma, Tensor? beta, Tensor scale, Tensor shift, "
@@ -644,6 +685,7 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("gelu_tanh", &gelu_tanh);
   m.impl("silu_mul", &silu_mul);
   m.impl("timestep_embedding", &timestep_embedding);
+  m.impl("timestep_mlp", &timestep_mlp);
   m.impl("rmsnorm_quant_fp8", &rmsnorm_quant_fp8);
   m.impl("norm_scale_shift_quant_fp8", &norm_scale_shift_quant_fp8);
 }

@@ -12,7 +12,7 @@ built extension raises ImportError exactly like the reference.
 
 New fused ops on the same path live in the same namespace
 (``qkv_norm_rope_pack``, ``gated_residual``, ``gated_residual_norm_scale_shift``,
-``gelu_tanh``, ``silu_mul``, ``timestep_embedding``, ``rmsnorm_quant_fp8``,
+``gelu_tanh``, ``silu_mul``, ``timestep_embedding``, ``timestep_mlp``, ``rmsnorm_quant_fp8``,
 ``norm_scale_shift_quant_fp8``).
 """
 import glob
@@ -44,6 +44,7 @@ __all__ = [
     "gelu_tanh",
     "silu_mul",
     "timestep_embedding",
+    "timestep_mlp",
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
     "qkv_norm_rope_pack_into",
@@ -158,6 +159,11 @@ def _fake_silu_mul(a, b):
 @torch.library.register_fake("joyomni_ops::timestep_embedding")
 def _fake_timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period):
     return t.new_empty((t.shape[0], dim), dtype=torch.float32)
+
+
+@torch.library.register_fake("joyomni_ops::timestep_mlp")
+def _fake_timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period):
+    return (w1.new_empty((t.shape[0], w3.shape[0])), w1.new_empty((t.shape[0], w1.shape[0])))
 
 
 @torch.library.register_fake("joyomni_ops::rmsnorm_quant_fp8")
@@ -276,6 +282,13 @@ def timestep_embedding(t, dim=256, flip_sin_to_cos=True, downscale_freq_shift=0.
                        max_period=10000.0):
     """Sinusoidal timestep projection (diffusers Timesteps), fp32 [B, dim]."""
     return _ops.timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period)
+
+
+def timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period=10000.0):
+    """WanTimeTextImageEmbedding timestep branch (dit.py:574-579, 605-620):
+    sinusoid(t) -> linear_1 -> SiLU -> linear_2 -> SiLU -> time_proj.
+    Returns (vec bf16 [B, proj_dim], silu(temb) bf16 [B, dim])."""
+    return _ops.timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period)
 
 
 def rmsnorm_quant_fp8(x, weight, eps=1e-6):

@@ -122,6 +122,32 @@ def timestep_embedding(t, dim=256, flip_sin_to_cos=True, downscale_freq_shift=0.
     return emb
 
 
+def linear_bf16(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor]) -> torch.Tensor:
+    """bf16 nn.Linear as the GPU reference runs it (cuBLAS): fp32 accumulation, bias
+    added in fp32, one rounding to bf16."""
+    y = x.float() @ w.float().t()
+    if b is not None:
+        y = y + b.float()
+    return y.to(torch.bfloat16)
+
+
+def silu_bf16(x: torch.Tensor) -> torch.Tensor:
+    """nn.SiLU on a bf16 tensor: fp32 math on the bf16 values, rounded to bf16."""
+    return F.silu(x.float()).to(torch.bfloat16)
+
+
+def timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period=10000.0):
+    """WanTimeTextImageEmbedding timestep branch (deploy/xvideo/models/dit/dit.py:574-579,
+    605-620): Timesteps(freq, flip_sin_to_cos=True, shift=0) -> bf16 -> time_embedder
+    (linear_1, SiLU, linear_2) -> act_fn SiLU -> time_proj.  Returns (vec, s1, s2) with
+    s1 = silu(linear_1(e)) and s2 = silu(temb), the two tensors the modules materialise
+    between the Linears."""
+    e = timestep_embedding(t, w1.shape[1], True, 0.0, 1.0, max_period).to(torch.bfloat16)
+    s1 = silu_bf16(linear_bf16(e, w1, b1))
+    s2 = silu_bf16(linear_bf16(s1, w2, b2))
+    return linear_bf16(s2, w3, b3), s1, s2
+
+
 # ----------------------------------------------------------------------------- q/k norm + rope
 def _rope_pairs(xn: torch.Tensor, c: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     x1, x2 = xn[..., 0::2], xn[..., 1::2]
