@@ -122,17 +122,24 @@ int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
     const int kb = nb <= 1 ? 1 : (nb <= 2 ? 2 : (nb <= 4 ? 4 : 8));
     const size_t smem = (size_t)kb * a.K * 2;
     const int64_t need = cdiv((int64_t)a.N * 32, (int64_t)kThreads);  // one warp per output row
-    auto go = [&](auto kern) {
+    auto go = [&](auto kern) -> int {
+      // the staged input rows take up to 8 x 4096 bf16 = 64 KB of shared memory
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return fail(JO_ERR_CUDA, "timestep_mlp: cannot reserve %zu bytes of shared memory", smem);
       // one wave: the resident CTAs walk the rows with a grid stride
       const int64_t cap = (int64_t)di->sm_count * std::max(1, occupancy((const void*)kern, kThreads, smem));
       kern<<<(unsigned)std::min(need, cap), kThreads, smem, st>>>(a, b0);
+      return JO_OK;
     };
+    int s = JO_OK;
     switch (kb) {
-      case 1: go(temb_layer_kernel<1, kSinIn, kSilu>); break;
-      case 2: go(temb_layer_kernel<2, kSinIn, kSilu>); break;
-      case 4: go(temb_layer_kernel<4, kSinIn, kSilu>); break;
-      default: go(temb_layer_kernel<8, kSinIn, kSilu>); break;
+      case 1: s = go(temb_layer_kernel<1, kSinIn, kSilu>); break;
+      case 2: s = go(temb_layer_kernel<2, kSinIn, kSilu>); break;
+      case 4: s = go(temb_layer_kernel<4, kSinIn, kSilu>); break;
+      default: s = go(temb_layer_kernel<8, kSinIn, kSilu>); break;
     }
+    if (s) return s;
     if (int s = after_launch("temb_layer_kernel")) return s;
   }
   return JO_OK;

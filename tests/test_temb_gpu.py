@@ -1,10 +1,13 @@
 """GPU parity of the timestep conditioning MLP (jo_timestep_mlp) against the oracle.
 
 Stage by stage on the GPU's own stage inputs (the two intermediates come back in
-the caller's scratch): each Linear(+SiLU) output within 1 bf16 ulp (fp32
-accumulation order differs).  The first stage also absorbs the sinusoid (CUDA
-sin/cos/exp vs the CPU's: an input element may differ by one bf16 ulp), so it is
-held to 2 ulps.  End to end: relative Frobenius error <= 1e-2.
+the caller's scratch): each Linear output within 1 bf16 ulp (fp32 accumulation
+order differs); a SiLU stage within 2 (the Linear's 1-ulp flip passes through SiLU,
+slope <= 1.1, before the second rounding).  The first stage's input is the sinusoid the kernel
+computes in its prologue with the arithmetic of jo_timestep_embedding, so that op's
+output (rounded to bf16) is the stage input; it is itself checked against the oracle
+sinusoid (|diff| <= 2e-4, CUDA vs CPU sin/cos/exp).  End to end: relative Frobenius
+error <= 1e-2.
 """
 import pytest
 import torch
@@ -39,7 +42,8 @@ def run_cabi(dev, t, ws, max_period=10000.0):
 
 
 @pytest.mark.parametrize("B,freq,dim,proj,bias", [(1, 256, 3072, 18432, True), (2, 256, 3072, 18432, True),
-                                                  (3, 256, 512, 1024, False), (9, 128, 264, 520, True)])
+                                                  (3, 256, 512, 1024, False), (9, 128, 264, 520, True),
+                                                  (16, 256, 4096, 1032, True)])
 def test_timestep_mlp(dev, B, freq, dim, proj, bias):
     g = torch.Generator().manual_seed(B + dim)
     t = torch.rand(B, generator=g) * 1000.0
@@ -47,8 +51,17 @@ def test_timestep_mlp(dev, B, freq, dim, proj, bias):
     w1, b1, w2, b2, w3, b3 = ws
     vec, s1, s2 = run_cabi(dev, t, ws)
     rvec, rs1, rs2 = ops.timestep_mlp(t, *ws)
-    assert_ulp_close(s1, rs1, 2.0, what="s1 = silu(linear_1(sinusoid))")
-    assert_ulp_close(s2, ops.silu_bf16(ops.linear_bf16(s1, w2, b2)), 1.0, what="s2 = silu(linear_2(s1))")
+    from joyomni_ops import cabi
+
+    e32 = torch.empty(B, freq, dtype=torch.float32, device=dev)
+    tg = t.float().to(dev)
+    cabi.call("jo_timestep_embedding", e32.data_ptr(), tg.data_ptr(), B, freq, 1, 0.0, 1.0, 10000.0, cabi.stream())
+    # the sinusoid itself: |diff| <= 2e-4 before rounding (two math libraries; t up
+    # to 1000 rad amplifies a 1-ulp exp difference), as in test_timestep_embedding
+    assert (e32.cpu() - ops.timestep_embedding(t, freq)).abs().max().item() <= 2e-4
+    e = e32.cpu().to(BF)
+    assert_ulp_close(s1, ops.silu_bf16(ops.linear_bf16(e, w1, b1)), 2.0, what="s1 = silu(linear_1(e))")
+    assert_ulp_close(s2, ops.silu_bf16(ops.linear_bf16(s1, w2, b2)), 2.0, what="s2 = silu(linear_2(s1))")
     assert_ulp_close(vec, ops.linear_bf16(s2, w3, b3), 1.0, what="vec = time_proj(s2)")
     rel = ((vec.float() - rvec.float()).norm() / rvec.float().norm()).item()
     assert rel < 1e-2, f"end to end rel err {rel}"
