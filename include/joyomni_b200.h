@@ -227,6 +227,19 @@ JO_API int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void*
                            const void* b3, int64_t proj_dim, void* scratch, int64_t scratch_bytes,
                            float max_period, void* stream);
 
+/* jo_timestep_mlp without the scratch argument, for callers that cannot
+ * allocate device memory.  No counterpart in the reference.  The two bf16
+ * intermediates go to a file-scope device array of 256 KB, so
+ * batch * dim <= 65536 (larger sizes return JO_ERR_SHAPE); nothing in it has to
+ * start at zero (every call writes s1 and s2 before reading them).  The array is
+ * shared by every call on a device: calls whose kernels overlap on the GPU (other
+ * streams, other threads) race on it.  The array's address is looked up with
+ * cudaGetSymbolAddress on the first call on each device (with that device
+ * current); make that first call before any stream capture.  Allocates nothing. */
+JO_API int jo_timestep_mlp_noalloc(void* vec, const float* t, int64_t batch, const void* w1, const void* b1,
+                                   int64_t freq_dim, int64_t dim, const void* w2, const void* b2, const void* w3,
+                                   const void* b3, int64_t proj_dim, float max_period, void* stream);
+
 /* RMSNorm -> per-token FP8 quant, one pass: y = dtype(rmsnorm(x)*w) is rounded
  * to dtype in registers, then quantised with the jo_per_token_quant_fp8
  * semantics.  Oracle: quant(_torch_rmsnorm(x, w, eps)). */

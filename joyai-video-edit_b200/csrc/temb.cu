@@ -21,6 +21,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -221,6 +222,44 @@ int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void* w1, co
                 (long long)scratch_bytes);
   return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
                           reinterpret_cast<__nv_bfloat16*>(scratch), max_period, (cudaStream_t)stream, di);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the scratch is a file-scope device array of a fixed
+// size, shared by every call on a device.
+constexpr int64_t kStaticScratchElems = 2 * 16 * 4096;  // s1 + s2 for batch * dim <= 65536 (256 KB)
+static __device__ __align__(256) __nv_bfloat16 g_temb_scratch[kStaticScratchElems];
+
+int jo_timestep_mlp_noalloc(void* vec, const float* t, int64_t batch, const void* w1, const void* b1,
+                            int64_t freq_dim, int64_t dim, const void* w2, const void* b2, const void* w3,
+                            const void* b3, int64_t proj_dim, float max_period, void* stream) {
+  const DeviceInfo* di;
+  if (int s = device_info(&di)) return s;
+  if (int s = timestep_mlp_check(vec, t, batch, w1, freq_dim, dim, w2, w3, proj_dim, max_period)) return s;
+  if (batch == 0) return JO_OK;
+  if (2 * batch * dim > kStaticScratchElems)
+    return fail(JO_ERR_SHAPE, "timestep_mlp_noalloc: batch * dim = %lld exceeds the static scratch limit of %lld",
+                (long long)(batch * dim), (long long)(kStaticScratchElems / 2));
+  // the array's address on the current device, looked up once per device
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(JO_ERR_CUDA, "timestep_mlp_noalloc: no current device");
+  void* ptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      const cudaError_t e = cudaGetSymbolAddress(&addr[dev], g_temb_scratch);
+      if (e != cudaSuccess) {
+        addr[dev] = nullptr;
+        return fail(JO_ERR_CUDA, "timestep_mlp_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      }
+    }
+    ptr = addr[dev];
+  }
+  return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
+                          reinterpret_cast<__nv_bfloat16*>(ptr), max_period, (cudaStream_t)stream, di);
 }
 
 }  // extern "C"
