@@ -511,7 +511,7 @@ def dist_init(n_gpus: int):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
@@ -666,16 +666,25 @@ def run_ours(args, wl: Workload):
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
         clocks.start()
-    # soak so the clock record covers >= ~1 s of this workload around the timed region
-    t_end = time.perf_counter() + 1.0
-    i = 0
-    while time.perf_counter() < t_end:
+    # soak so the clock record covers >= ~1 s of this workload around the timed region;
+    # every rank runs the same number of soak iterations (the chain's steps carry
+    # collectives), agreed as the max over ranks of each rank's own estimate
+    def soak_iter(i):
         if graph is not None:
             graph.replay()
         else:
             step(i)
-        i += 1
-        if i % 16 == 0:
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(2):
+        soak_iter(i)
+    torch.cuda.synchronize()
+    per_iter = max((time.perf_counter() - t0) / 2, 1e-6)
+    n_soak = int(max_over_ranks(float(min(4096, int(1.0 / per_iter) + 1)), world))
+    for i in range(n_soak):
+        soak_iter(i)
+        if i % 16 == 15:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
     if graph is not None:
