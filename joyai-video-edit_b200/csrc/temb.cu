@@ -12,10 +12,11 @@
 //
 // Design (B200): at the model's batch (1-2 timesteps) every layer is a GEMV
 // bound by the weight read (W3 alone is 113 MB at dim 3072), so each layer is
-// one HBM stream: a warp owns one output row at a time, issues all of its 16-byte
-// weight loads (up to 4096 elements) before the first use, and multiplies them
-// against the batch's input rows staged once per CTA in shared memory; one warp
-// shuffle reduction per batch row.  The two intermediates live in caller-owned
+// one HBM stream: each CTA (one per SM) owns a contiguous block of output rows,
+// its 16 warps stream ~6 KB units of consecutive weight rows through their own
+// shared-memory slots with TMA bulk copies (bounded mbarrier waits), and
+// multiply them against the batch's input rows staged once per CTA in shared
+// memory; one warp shuffle reduction per output row and batch row.  The two intermediates live in caller-owned
 // scratch (4 * B * dim bytes) between the launches; the sinusoid is computed in
 // the first layer's prologue.
 #include <math.h>
@@ -23,14 +24,16 @@
 #include <algorithm>
 #include <mutex>
 
-#include "common.cuh"
+#include "pipeline.cuh"
 
 namespace jo {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kMaxK = 4096;            // input features per layer (16 x 256)
-constexpr int kJ = kMaxK / 256;         // 16-byte weight vectors per lane per row
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kMaxK = 4096;                 // input features per layer
+constexpr int kMaxB = 8;                    // batch rows per launch
+constexpr uint32_t kBudget = 216u * 1024u;  // shared memory: batch rows + weight slots
 
 struct TembLayer {
   const __nv_bfloat16* x;  // [B, K] input rows (null for the sinusoid layer)
@@ -42,14 +45,53 @@ struct TembLayer {
   float neg_log_period;    // -ln(max_period) rounded to fp32
 };
 
+struct TembCfg {
+  int rows_per_unit;    // consecutive weight rows per bulk copy
+  int m;                // slots per warp
+  uint32_t slot_bytes;  // rows_per_unit * K * 2, rounded up to 128
+  uint32_t x_off;       // byte offset of the staged batch rows
+  uint32_t data_off;    // byte offset of slot 0
+};
+
 __device__ __forceinline__ float silu_exact(float v) { return v / (1.f + expf(-v)); }
 
-// One layer for batch rows [b0, b0 + kB) (rows >= B are skipped).
+// One layer for batch rows [b0, b0 + kB) (rows >= B are skipped).  Weight rows
+// stream through per-warp shared-memory slots filled with 1-D TMA bulk copies
+// (each warp keeps its next m units in flight; the copy engine holds the bytes,
+// not registers), as in the staged row kernels.
 template <int kB, bool kSinIn, bool kSilu>
-__global__ void __launch_bounds__(kThreads) temb_layer_kernel(const TembLayer a, int b0) {
-  extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [kB, K]
+__global__ void __launch_bounds__(kThreads, 1)
+    temb_layer_kernel(const TembLayer a, const TembCfg cfg, int b0, unsigned int* fault) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   const int K = a.K;
-  // ---- stage the batch's input rows
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem_raw);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw + cfg.x_off);  // [kB, K]
+  const int m = cfg.m, R = cfg.rows_per_unit;
+  const int64_t per = (a.N + gridDim.x - 1) / gridDim.x;  // rows of this CTA
+  const int64_t r0 = (int64_t)blockIdx.x * per;
+  const int64_t rend = r0 + per < a.N ? r0 + per : a.N;
+  const int nrows = rend > r0 ? (int)(rend - r0) : 0;
+  const int units = (nrows + R - 1) / R;
+  if (threadIdx.x < kWarps * m) mbar_init(base + 8u * threadIdx.x, 1);
+  if (threadIdx.x == 0) mbar_init_fence();
+  __syncthreads();
+  const uint32_t bar0 = base + 8u * (uint32_t)(warp * m);
+  const uint32_t slot0 = base + cfg.data_off + (uint32_t)(warp * m) * cfg.slot_bytes;
+  auto unit_rows = [&](int u) { return min(R, nrows - u * R); };
+  // unit k of this warp is unit warp + k * kWarps of the CTA, in slot k % m
+  auto issue = [&](int k) {
+    const int u = warp + k * kWarps;
+    if (u >= units) return;
+    const uint32_t bytes = (uint32_t)unit_rows(u) * (uint32_t)K * 2u;
+    const uint32_t bar = bar0 + 8u * (uint32_t)(k % m);
+    mbar_expect_tx(bar, bytes);
+    bulk_load(slot0 + (uint32_t)(k % m) * cfg.slot_bytes, a.w + (r0 + (int64_t)u * R) * K, bytes, bar);
+  };
+  if (lane == 0)
+    for (int k = 0; k < m; ++k) issue(k);
+
+  // ---- stage the batch's input rows while the first weight rows are in flight
   if constexpr (kSinIn) {
     // diffusers get_timestep_embedding with flip_sin_to_cos=True, shift 0:
     // [cos(t f_i), sin(t f_i)], f_i = exp(-ln(P) * i / half), fp32, then bf16
@@ -76,72 +118,98 @@ __global__ void __launch_bounds__(kThreads) temb_layer_kernel(const TembLayer a,
   }
   __syncthreads();
 
-  const int lane = threadIdx.x & 31;
-  const int warps = (int)(gridDim.x * kThreads / 32);
-  for (int n = (int)(blockIdx.x * kThreads + threadIdx.x) / 32; n < a.N; n += warps) {
-    const __nv_bfloat16* wr = a.w + (int64_t)n * K;
-    uint4 w[kJ];
+  int k = 0;
+  for (; warp + k * kWarps < units; ++k) {
+    const int u = warp + k * kWarps;
+    const uint32_t sl = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
+    if (!mbar_wait(bar0 + 8u * (uint32_t)(k % m), (uint32_t)((k / m) & 1), fault)) break;
+    const int nr = unit_rows(u);
+    for (int r = 0; r < nr; ++r) {
+      float acc[kB];
 #pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-      const int k = j * 256 + lane * 8;
-      w[j] = k < K ? ld_stream(wr + k) : make_uint4(0, 0, 0, 0);
-    }
-    float acc[kB];
+      for (int b = 0; b < kB; ++b) acc[b] = 0.f;
+      for (int kk = lane * 8; kk < K; kk += 256) {
+        float wf[8];
+        Elt<__nv_bfloat16>::unpack(lds128(sl + (uint32_t)(r * K + kk) * 2u), wf);
 #pragma unroll
-    for (int b = 0; b < kB; ++b) acc[b] = 0.f;
-#pragma unroll
-    for (int j = 0; j < kJ; ++j) {
-      const int k = j * 256 + lane * 8;
-      if (k >= K) continue;
-      float wf[8];
-      Elt<__nv_bfloat16>::unpack(w[j], wf);
+        for (int b = 0; b < kB; ++b) {
+          float xf[8];
+          Elt<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(xs + b * K + kk), xf);
+          float p0 = wf[0] * xf[0], p1 = wf[1] * xf[1];
+          p0 = fmaf(wf[2], xf[2], p0);
+          p1 = fmaf(wf[3], xf[3], p1);
+          p0 = fmaf(wf[4], xf[4], p0);
+          p1 = fmaf(wf[5], xf[5], p1);
+          p0 = fmaf(wf[6], xf[6], p0);
+          p1 = fmaf(wf[7], xf[7], p1);
+          acc[b] += p0 + p1;
+        }
+      }
+      const int64_t n = r0 + (int64_t)u * R + r;
+      const float bias = a.bias ? __bfloat162float(a.bias[n]) : 0.f;
 #pragma unroll
       for (int b = 0; b < kB; ++b) {
-        float xf[8];
-        Elt<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(xs + b * K + k), xf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[b] = fmaf(wf[e], xf[e], acc[b]);
+        const float h = warp_sum(acc[b]) + bias;
+        if (lane == b && b0 + b < a.B) {
+          float y = __bfloat162float(__float2bfloat16_rn(h));
+          if constexpr (kSilu) y = silu_exact(y);
+          a.y[(int64_t)(b0 + b) * a.N + n] = __float2bfloat16_rn(y);
+        }
       }
     }
-    const float bias = a.bias ? __bfloat162float(a.bias[n]) : 0.f;
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const float h = warp_sum(acc[b]) + bias;
-      if (lane == b && b0 + b < a.B) {
-        float y = __bfloat162float(__float2bfloat16_rn(h));
-        if constexpr (kSilu) y = silu_exact(y);
-        a.y[(int64_t)(b0 + b) * a.N + n] = __float2bfloat16_rn(y);
-      }
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // slot reads before the refill
+      issue(k + m);
     }
   }
+  // error path only (a wait expired at unit k): copies issued for later units must land
+  if (lane == 0 && warp + k * kWarps < units)
+    for (int j = k + 1; j < k + m && warp + j * kWarps < units; ++j)
+      mbar_wait(bar0 + 8u * (uint32_t)(j % m), (uint32_t)((j / m) & 1), fault);
+}
+
+template <int kB, bool kSinIn, bool kSilu>
+int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, size_t smem, cudaStream_t st,
+               const DeviceInfo* di) {
+  auto kern = temb_layer_kernel<kB, kSinIn, kSilu>;
+  static bool attr = false;  // one per kernel instantiation
+  if (!attr) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget) != cudaSuccess)
+      return fail(JO_ERR_CUDA, "timestep_mlp: cannot reserve shared memory");
+    attr = true;
+  }
+  kern<<<(unsigned)grid, kThreads, smem, st>>>(a, cfg, b0, di->fault);
+  return JO_OK;
 }
 
 template <bool kSinIn, bool kSilu>
 int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
-  for (int b0 = 0; b0 < a.B; b0 += 8) {
-    const int nb = std::min(8, a.B - b0);
+  for (int b0 = 0; b0 < a.B; b0 += kMaxB) {
+    const int nb = std::min(kMaxB, a.B - b0);
     const int kb = nb <= 1 ? 1 : (nb <= 2 ? 2 : (nb <= 4 ? 4 : 8));
-    const size_t smem = (size_t)kb * a.K * 2;
-    const int64_t need = cdiv((int64_t)a.N * 32, (int64_t)kThreads);  // one warp per output row
-    auto go = [&](auto kern) -> int {
-      // the staged input rows take up to 8 x 4096 bf16 = 64 KB of shared memory
-      if (smem > 48 * 1024 &&
-          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return fail(JO_ERR_CUDA, "timestep_mlp: cannot reserve %zu bytes of shared memory", smem);
-      // one wave: the resident CTAs walk the rows with a grid stride
-      const int64_t cap = (int64_t)di->sm_count * std::max(1, occupancy((const void*)kern, kThreads, smem));
-      kern<<<(unsigned)std::min(need, cap), kThreads, smem, st>>>(a, b0);
-      return JO_OK;
-    };
+    TembCfg cfg{};
+    const uint32_t row_bytes = (uint32_t)a.K * 2u;
+    cfg.rows_per_unit = std::max(1, (int)(6144u / row_bytes));  // ~6 KB per bulk copy
+    cfg.slot_bytes = ((uint32_t)cfg.rows_per_unit * row_bytes + 127u) & ~127u;
+    cfg.x_off = 1024;  // after the warps' mbarriers
+    cfg.data_off = (cfg.x_off + (uint32_t)kb * row_bytes + 127u) & ~127u;
+    const uint32_t avail = kBudget - cfg.data_off;
+    cfg.m = (int)std::min<uint32_t>(3u, avail / (kWarps * cfg.slot_bytes));
+    if (cfg.m < 1) return fail(JO_ERR_SHAPE, "timestep_mlp: rows too large to stage");
+    const size_t smem = cfg.data_off + (size_t)kWarps * cfg.m * cfg.slot_bytes;
+    // CTAs: one per SM (fewer only when there are fewer units than SMs)
+    const int64_t units = cdiv(a.N, cfg.rows_per_unit);
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(di->sm_count, units));
     int s = JO_OK;
     switch (kb) {
-      case 1: s = go(temb_layer_kernel<1, kSinIn, kSilu>); break;
-      case 2: s = go(temb_layer_kernel<2, kSinIn, kSilu>); break;
-      case 4: s = go(temb_layer_kernel<4, kSinIn, kSilu>); break;
-      default: s = go(temb_layer_kernel<8, kSinIn, kSilu>); break;
+      case 1: s = launch_one<1, kSinIn, kSilu>(a, cfg, b0, grid, smem, st, di); break;
+      case 2: s = launch_one<2, kSinIn, kSilu>(a, cfg, b0, grid, smem, st, di); break;
+      case 4: s = launch_one<4, kSinIn, kSilu>(a, cfg, b0, grid, smem, st, di); break;
+      default: s = launch_one<8, kSinIn, kSilu>(a, cfg, b0, grid, smem, st, di); break;
     }
     if (s) return s;
-    if (int s = after_launch("temb_layer_kernel")) return s;
+    if (int e = after_launch("temb_layer_kernel")) return e;
   }
   return JO_OK;
 }
