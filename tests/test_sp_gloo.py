@@ -30,7 +30,7 @@ def _worker(rank, world, port, mode, q):
     try:
         sys.path[:0] = [str(REPO), str(REPO / "joyai-video-edit_b200")]
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-        timeout = datetime.timedelta(seconds=5 if mode == "absent" else 60)
+        timeout = datetime.timedelta(seconds=60 if mode == "ok" else 5)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
         from joyomni_ops import chain
 
@@ -47,6 +47,11 @@ def _worker(rank, world, port, mode, q):
         if mode == "absent" and rank == 1:
             q.put((rank, "skipped"))
             return  # never joins the collective
+        if mode == "killed" and rank == 1:
+            os._exit(17)  # the process dies between steps, with nothing in flight
+        if mode == "mismatch" and rank == 1:
+            # a rank whose buffers were sized for a different chunk length
+            bufs = chain.KVBuffers(cache, img + 2 * world, txt, H, D, world, "cpu", dtype=torch.float32)
         chain.gather_chunk_kv(bufs, rank, None)
         full = torch.arange(img, dtype=torch.float32).view(-1, 1, 1).expand(-1, H, D)
         assert torch.equal(bufs.k[bufs.chunk_kv_rows()], full)
@@ -74,6 +79,7 @@ def _run(mode, world=2):
     while not q.empty():
         r, msg = q.get()
         res[r] = msg
+    _run.exitcodes = [p.exitcode for p in procs]
     return res, alive
 
 
@@ -96,3 +102,20 @@ def test_absent_rank_fails_cleanly():
     assert not alive, "a rank hung"
     assert res.get(1) == "skipped"
     assert res.get(0, "").startswith("error"), res
+
+
+def test_killed_rank_fails_cleanly():
+    """A rank that dies (process exit) between steps: the survivor's next collective
+    ends with an error within the process-group timeout instead of hanging."""
+    res, alive = _run("killed")
+    assert not alive, "a rank hung"
+    assert _run.exitcodes[1] == 17, _run.exitcodes
+    assert res.get(0, "").startswith("error"), res
+
+
+def test_mismatched_shapes_fail_cleanly():
+    """Ranks whose K/V buffers disagree on the chunk length: the all-gather reports an
+    error on every rank (or times out with one) instead of hanging or writing garbage."""
+    res, alive = _run("mismatch")
+    assert not alive, "a rank hung"
+    assert all(str(res.get(r, "error")).startswith("error") for r in (0, 1)), res
