@@ -148,6 +148,18 @@ JO_API int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, co
                      const void* bias, int64_t m, int64_t n, int64_t k, int out_dtype,
                      void* stream);
 
+/* FP8 GEMM with the gated residual in the epilogue:
+ *   D = residual + gate[n] * ((A.B) * sB[n] * sA[m] (+ bias[n]))
+ * the down-projection + gated residual of each MLP (dit.py:536-538:
+ * Fp8Linear, then sgl_fused_ops.fused_add_gate = torch.addcmul(res, x, gate)) in
+ * one pass: the product is not rounded to D's dtype before the residual.
+ * residual [M, N] (row stride ldr), gate [N], both of D's dtype; D may alias
+ * residual (same rows, same stride).  Other arguments as jo_fp8_scaled_mm. */
+JO_API int jo_fp8_scaled_mm_gated_residual(void* d, int64_t ldd, const void* a, int64_t lda, const void* b,
+                                           int64_t ldb, const float* scale_a, const float* scale_b, const void* bias,
+                                           const void* residual, int64_t ldr, const void* gate, int64_t m, int64_t n,
+                                           int64_t k, int out_dtype, void* stream);
+
 /* ====================================================================== *
  *  New fused ops on the same path (no single reference kernel)
  * ====================================================================== */

@@ -112,10 +112,18 @@ struct GemmArgs {
   const float* sa;
   const float* sb;
   const void* bias;
+  const void* res;   // kEpiResid: residual [M, N] (row stride ldr), same dtype as D
+  int64_t ldr;
+  const void* gate;  // kEpiResid: gate [N], same dtype as D
   int m, n, k;
   int tiles_m, tiles_n;
   unsigned int* fault;
 };
+
+// Epilogue variants: + bias[n]; gated residual D = res + gate[n] * (GEMM result)
+// (torch.addcmul(res, x, gate) of sgl_fused_ops.py:302-305 applied to the fp32
+// result, dit.py:536-538) instead of rounding the product to D's dtype first.
+enum GemmEpi { kEpiBias = 1, kEpiResid = 2 };
 
 template <typename OutT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -128,7 +136,7 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return pack_f16x2(a, b);
 }
 
-template <typename OutT, bool kBias>
+template <typename OutT, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const GemmArgs args) {
@@ -251,8 +259,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    constexpr bool kBias = (kEpi & kEpiBias) != 0, kResid = (kEpi & kEpiResid) != 0;
     OutT* D = reinterpret_cast<OutT*>(args.d);
     const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
+    const OutT* gate = reinterpret_cast<const OutT*>(args.gate);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
       if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
@@ -261,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < args.m;
       const float s_a = row_ok ? __ldg(args.sa + row) : 0.f;
       OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
+      const OutT* rrow = reinterpret_cast<const OutT*>(args.res) + (int64_t)(row_ok ? row : 0) * args.ldr;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -289,6 +300,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
           }
           if (row_ok) {
+            if constexpr (kResid) {
+              float rv[8], gv[8];
+              // plain (coherent) load: D may alias the residual
+              Elt<OutT>::unpack(*reinterpret_cast<const uint4*>(rrow + ng), rv);
+              Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(gate + ng)), gv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = fmaf(gv[e], o[e], rv[e]);
+            }
             uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
                                  pack2<OutT>(o[6], o[7]));
             *reinterpret_cast<uint4*>(drow + ng) = v;
@@ -381,7 +400,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
 constexpr int kP_EpiWarps = 8;                     // 2 per TMEM lane quadrant, 128 columns each
 constexpr int kP_Threads = 64 + 32 * kP_EpiWarps;  // producer warp, MMA warp, epilogue warps
 
-template <typename OutT, bool kBias>
+template <typename OutT, int kEpi>
 __global__ void __launch_bounds__(kP_Threads, 1)
     fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                          const GemmArgs args) {
@@ -518,8 +537,10 @@ __global__ void __launch_bounds__(kP_Threads, 1)
     const int q = warp & 3, half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
+    constexpr bool kBias = (kEpi & kEpiBias) != 0, kResid = (kEpi & kEpiResid) != 0;
     OutT* D = reinterpret_cast<OutT*>(args.d);
     const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
+    const OutT* gate = reinterpret_cast<const OutT*>(args.gate);
     for (int tile = cluster; tile < num_tiles; tile += nclusters) {
       const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
       if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
@@ -528,6 +549,7 @@ __global__ void __launch_bounds__(kP_Threads, 1)
       const bool row_ok = row < args.m;
       const float s_a = row_ok ? __ldg(args.sa + row) : 0.f;
       OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
+      const OutT* rrow = reinterpret_cast<const OutT*>(args.res) + (int64_t)(row_ok ? row : 0) * args.ldr;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kP_BN);
 #pragma unroll 1
       for (int c = half * (kP_BN / 64); c < (half + 1) * (kP_BN / 64); ++c) {
@@ -556,6 +578,14 @@ __global__ void __launch_bounds__(kP_Threads, 1)
             o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
           }
           if (row_ok) {
+            if constexpr (kResid) {
+              float rv[8], gv[8];
+              // plain (coherent) load: D may alias the residual
+              Elt<OutT>::unpack(*reinterpret_cast<const uint4*>(rrow + ng), rv);
+              Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(gate + ng)), gv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = fmaf(gv[e], o[e], rv[e]);
+            }
             uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
                                  pack2<OutT>(o[6], o[7]));
             *reinterpret_cast<uint4*>(drow + ng) = v;
@@ -613,10 +643,10 @@ int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_t
   return JO_OK;
 }
 
-template <typename OutT, bool kBias>
+template <typename OutT, int kEpi>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st,
                 const DeviceInfo* di) {
-  auto kern = fp8_gemm_kernel<OutT, kBias>;
+  auto kern = fp8_gemm_kernel<OutT, kEpi>;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
@@ -630,9 +660,9 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
 }
 
 // CTA-pair launch: clusters of (2,1,1), as many as can be resident at once.
-template <typename OutT, bool kBias>
+template <typename OutT, int kEpi>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st) {
-  auto kern = fp8_gemm_pair_kernel<OutT, kBias>;
+  auto kern = fp8_gemm_pair_kernel<OutT, kEpi>;
   static int max_clusters = 0;
   if (!max_clusters) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kP_SmemBytes) != cudaSuccess)
@@ -674,14 +704,22 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
 }  // namespace
 }  // namespace jo
 
-using namespace jo;
+namespace jo {
+namespace {
 
-extern "C" {
+template <int kEpi>
+int dispatch_gemm(bool pair, int out_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
+                  cudaStream_t st, const DeviceInfo* di) {
+  if (pair)
+    return out_dtype == JO_BF16 ? launch_gemm_pair<__nv_bfloat16, kEpi>(ma, mb, g, st)
+                                : launch_gemm_pair<__half, kEpi>(ma, mb, g, st);
+  return out_dtype == JO_BF16 ? launch_gemm<__nv_bfloat16, kEpi>(ma, mb, g, st, di)
+                              : launch_gemm<__half, kEpi>(ma, mb, g, st, di);
+}
 
-int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
-                     const float* scale_a, const float* scale_b, const void* bias, int64_t m, int64_t n,
-                     int64_t k, int out_dtype, void* stream) {
-  const char* op = "fp8_scaled_mm";
+int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
+               const float* scale_a, const float* scale_b, const void* bias, const void* res, int64_t ldr,
+               const void* gate, int64_t m, int64_t n, int64_t k, int out_dtype, void* stream) {
   const DeviceInfo* di;
   if (int s = device_info(&di)) return s;
   if (m < 0 || n < 0 || k < 0) return fail(JO_ERR_SHAPE, "%s: negative size", op);
@@ -706,6 +744,9 @@ int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const voi
   g.sa = scale_a;
   g.sb = scale_b;
   g.bias = bias;
+  g.res = res;
+  g.ldr = ldr;
+  g.gate = gate;
   g.m = (int)m;
   g.n = (int)n;
   g.k = (int)k;
@@ -714,14 +755,39 @@ int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const voi
   g.fault = di->fault;
   if ((int64_t)g.tiles_m * g.tiles_n > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many tiles", op);
   cudaStream_t st = (cudaStream_t)stream;
-  if (pair) {
-    if (out_dtype == JO_BF16)
-      return bias ? launch_gemm_pair<__nv_bfloat16, true>(ma, mb, g, st) : launch_gemm_pair<__nv_bfloat16, false>(ma, mb, g, st);
-    return bias ? launch_gemm_pair<__half, true>(ma, mb, g, st) : launch_gemm_pair<__half, false>(ma, mb, g, st);
+  const int epi = (bias ? kEpiBias : 0) | (res ? kEpiResid : 0);
+  switch (epi) {
+    case 0: return dispatch_gemm<0>(pair, out_dtype, ma, mb, g, st, di);
+    case kEpiBias: return dispatch_gemm<kEpiBias>(pair, out_dtype, ma, mb, g, st, di);
+    case kEpiResid: return dispatch_gemm<kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
+    default: return dispatch_gemm<kEpiBias | kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
   }
-  if (out_dtype == JO_BF16)
-    return bias ? launch_gemm<__nv_bfloat16, true>(ma, mb, g, st, di) : launch_gemm<__nv_bfloat16, false>(ma, mb, g, st, di);
-  return bias ? launch_gemm<__half, true>(ma, mb, g, st, di) : launch_gemm<__half, false>(ma, mb, g, st, di);
+}
+
+}  // namespace
+}  // namespace jo
+
+using namespace jo;
+
+extern "C" {
+
+int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
+                     const float* scale_a, const float* scale_b, const void* bias, int64_t m, int64_t n,
+                     int64_t k, int out_dtype, void* stream) {
+  return gemm_entry("fp8_scaled_mm", d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, nullptr, 0, nullptr, m, n, k,
+                    out_dtype, stream);
+}
+
+int jo_fp8_scaled_mm_gated_residual(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
+                                    const float* scale_a, const float* scale_b, const void* bias,
+                                    const void* residual, int64_t ldr, const void* gate, int64_t m, int64_t n,
+                                    int64_t k, int out_dtype, void* stream) {
+  const char* op = "fp8_scaled_mm_gated_residual";
+  if (!residual || !gate) return fail(JO_ERR_INVALID, "%s: null residual or gate", op);
+  if (ldr < n || ldr % 8) return fail(JO_ERR_ALIGN, "%s: residual row stride must be >= N and a multiple of 8", op);
+  if (!aligned16(residual) || !aligned16(gate)) return fail(JO_ERR_ALIGN, "%s: residual and gate must be 16-byte aligned", op);
+  return gemm_entry(op, d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, residual, ldr, gate, m, n, k, out_dtype,
+                    stream);
 }
 
 }  // extern "C"

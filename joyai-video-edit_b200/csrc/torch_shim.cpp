@@ -326,6 +326,46 @@ torch::Tensor fp8_scaled_mm(const torch::Tensor& mat_a, const torch::Tensor& mat
 }
 
 // ------------------------------------------------------------------ new fused ops
+// fp8_scaled_mm + torch.addcmul(residual, ., gate) in the GEMM epilogue (dit.py:536-538).
+torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const torch::Tensor& mat_b,
+                                           const torch::Tensor& scales_a, const torch::Tensor& scales_b,
+                                           const torch::ScalarType& out_dtype, const c10::optional<torch::Tensor>& bias,
+                                           const torch::Tensor& residual, const torch::Tensor& gate) {
+  TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "mat_a and mat_b must be CUDA tensors");
+  TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 2, "mat_a and mat_b must be 2D tensors");
+  TORCH_CHECK(mat_a.stride(1) == 1, "mat_a must be a row major tensor");
+  TORCH_CHECK(mat_b.stride(0) == 1, "mat_b must be a column major tensor");
+  TORCH_CHECK(mat_a.size(1) == mat_b.size(0), "mat_a and mat_b shapes cannot be multiplied");
+  TORCH_CHECK(mat_a.scalar_type() == torch::kFloat8_e4m3fn && mat_b.scalar_type() == torch::kFloat8_e4m3fn,
+              "mat_a and mat_b must be Float8_e4m3fn");
+  TORCH_CHECK(out_dtype == torch::kHalf || out_dtype == torch::kBFloat16, "out_dtype must be Half or BFloat16");
+  TORCH_CHECK(scales_a.numel() == mat_a.size(0) && scales_a.is_contiguous() &&
+                  scales_a.scalar_type() == torch::kFloat32,
+              "scales_a must be contiguous Float32 with one value per row of mat_a");
+  TORCH_CHECK(scales_b.numel() == mat_b.size(1) && scales_b.is_contiguous() &&
+                  scales_b.scalar_type() == torch::kFloat32,
+              "scales_b must be contiguous Float32 with one value per column of mat_b");
+  if (bias) {
+    TORCH_CHECK(bias->numel() == mat_b.size(1) && bias->is_contiguous() && bias->dtype() == out_dtype,
+                "bias must be contiguous [N] of the output dtype");
+  }
+  const int64_t M = mat_a.size(0), N = mat_b.size(1);
+  TORCH_CHECK(residual.is_cuda() && residual.dim() == 2 && residual.size(0) == M && residual.size(1) == N &&
+                  residual.stride(1) == 1 && residual.scalar_type() == out_dtype,
+              "residual must be [M, N] of the output dtype with contiguous rows");
+  TORCH_CHECK(gate.is_cuda() && gate.numel() == N && gate.is_contiguous() && gate.scalar_type() == out_dtype,
+              "gate must be contiguous [N] (or [1, N]) of the output dtype");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  torch::Tensor out = torch::empty({M, N}, mat_a.options().dtype(out_dtype));
+  jo_check(jo_fp8_scaled_mm_gated_residual(out.data_ptr(), out.stride(0), mat_a.data_ptr(), mat_a.stride(0),
+                                           mat_b.data_ptr(), mat_b.stride(1), scales_a.data_ptr<float>(),
+                                           scales_b.data_ptr<float>(), bias ? bias->data_ptr() : nullptr,
+                                           residual.data_ptr(), residual.stride(0), gate.data_ptr(), M, N,
+                                           mat_a.size(1), dt_code(out_dtype), stream_of(mat_a)),
+           "fp8_scaled_mm_gated_residual");
+  return out;
+}
+
 
 torch::Tensor as_rows(const torch::Tensor& t, int64_t cols, const char* name) {
   TORCH_CHECK(t.size(-1) == cols, name, " last dim must be ", cols);
@@ -641,6 +681,9 @@ TORCH_LIBRARY(joyomni_ops, m) {
       "ScalarType out_dtype, Tensor? bias) -> Tensor");
   // New fused ops on the same path.
   m.def(
+      "fp8_scaled_mm_gated_residual(Tensor mat_a, Tensor mat_b, Tensor scales_a, Tensor scales_b, "
+      "ScalarType out_dtype, Tensor? bias, Tensor residual, Tensor gate) -> Tensor");
+  m.def(
       "qkv_norm_rope_pack(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
       "Tensor? sin, float eps, bool head_major, Tensor(a!)? k_pre_rope) -> (Tensor, Tensor, Tensor)");
   m.def(
@@ -676,6 +719,7 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("rmsnorm", &rmsnorm);
   m.impl("sgl_per_token_quant_fp8", &sgl_per_token_quant_fp8);
   m.impl("fp8_scaled_mm", &fp8_scaled_mm);
+  m.impl("fp8_scaled_mm_gated_residual", &fp8_scaled_mm_gated_residual);
   m.impl("qkv_norm_rope_pack", &qkv_norm_rope_pack);
   m.impl("qkv_norm_rope_pack_into", &qkv_norm_rope_pack_into);
   m.impl("gelu_quant_fp8", &gelu_quant_fp8);

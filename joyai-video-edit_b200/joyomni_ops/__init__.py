@@ -45,6 +45,7 @@ __all__ = [
     "silu_mul",
     "timestep_embedding",
     "timestep_mlp",
+    "fp8_scaled_mm_gated_residual",
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
     "qkv_norm_rope_pack_into",
@@ -159,6 +160,11 @@ def _fake_silu_mul(a, b):
 @torch.library.register_fake("joyomni_ops::timestep_embedding")
 def _fake_timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period):
     return t.new_empty((t.shape[0], dim), dtype=torch.float32)
+
+
+@torch.library.register_fake("joyomni_ops::fp8_scaled_mm_gated_residual")
+def _fake_fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate):
+    return mat_a.new_empty((mat_a.shape[0], mat_b.shape[1]), dtype=out_dtype)
 
 
 @torch.library.register_fake("joyomni_ops::timestep_mlp")
@@ -282,6 +288,12 @@ def timestep_embedding(t, dim=256, flip_sin_to_cos=True, downscale_freq_shift=0.
                        max_period=10000.0):
     """Sinusoidal timestep projection (diffusers Timesteps), fp32 [B, dim]."""
     return _ops.timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scale, max_period)
+
+
+def fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate):
+    """residual + gate * fp8_scaled_mm(...) with the residual in the GEMM epilogue
+    (dit.py:536-538: the down-projection and ``fused_add_gate`` in one pass)."""
+    return _ops.fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate)
 
 
 def timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period=10000.0):

@@ -12,7 +12,7 @@ fused sm_100a ops of this package:
     img/txt: attn quant + out-proj GEMM          sgl_per_token_quant_fp8, fp8_scaled_mm
              gated residual + LN2 + mod + quant  gated_residual_norm_scale_shift_quant_fp8 (dit.py:525-535)
              MLP up GEMM, GELU-tanh + quant      fp8_scaled_mm, gelu_quant_fp8   (dit.py:508-513)
-             MLP down GEMM, gated residual       fp8_scaled_mm, gated_residual   (dit.py:536-538)
+             MLP down GEMM + gated residual      fp8_scaled_mm_gated_residual    (dit.py:536-538)
 
 Sequence parallel: the video tokens of the chunk are sharded over the ranks of
 ``group``; each rank writes its K/V rows into its slice of the persistent KV
@@ -174,12 +174,12 @@ def _stream_out(x, attn, w: StreamWeights, m, trace=None, tag=""):
     h, hq, hs = jo.gated_residual_norm_scale_shift_quant_fp8(x, proj, gate1, scale2, shift2, "layer", 1e-6)
     up = w.up(hq, hs)
     gq, gs = jo.gelu_quant_fp8(up)
-    down = w.down(gq, gs)
-    out = jo.gated_residual(h, down, gate2)
+    # down projection with the gated residual in the GEMM epilogue
+    out = jo.fp8_scaled_mm_gated_residual(gq, w.down.wq, gs, w.down.ws, BF16, w.down.bias, h, gate2)
     if trace is not None:
         trace.update({f"{tag}.attn": attn, f"{tag}.aq": aq, f"{tag}.as": asc, f"{tag}.proj": proj, f"{tag}.h": h,
                       f"{tag}.hq": hq, f"{tag}.hs": hs, f"{tag}.up": up, f"{tag}.gq": gq, f"{tag}.gs": gs,
-                      f"{tag}.down": down, f"{tag}.out": out})
+                      f"{tag}.out": out})
     return out
 
 

@@ -122,6 +122,17 @@ def timestep_embedding(t, dim=256, flip_sin_to_cos=True, downscale_freq_shift=0.
     return emb
 
 
+def fp8_scaled_mm_gated_residual(a_q, b_q, scale_a, scale_b, bias, residual, gate) -> torch.Tensor:
+    """residual + gate * (the fp8_scaled_mm result before its rounding): the down
+    projection and torch.addcmul(res, x, gate) (dit.py:536-538, sgl_fused_ops.py:302-305)
+    with the product kept in fp32, one rounding to the residual's dtype."""
+    acc = (a_q.double() @ b_q.double()).float()
+    d = (acc * scale_b.reshape(1, -1).float()) * scale_a.reshape(-1, 1).float()
+    if bias is not None:
+        d = d + bias.float().reshape(1, -1)
+    return (residual.float() + gate.float().reshape(1, -1) * d).to(residual.dtype)
+
+
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor]) -> torch.Tensor:
     """bf16 nn.Linear as the GPU reference runs it (cuBLAS): fp32 accumulation, bias
     added in fp32, one rounding to bf16."""

@@ -152,9 +152,9 @@ def test_block_chain(dev, hidden, heads, ffn, img_len, txt_len, cache_len):
         gemm_close(T[f"{tag}.proj"], ops.fp8_linear(T[f"{tag}.aq"], T[f"{tag}.as"], ws.proj), f"{tag} proj")
         assert_ulp_close(T[f"{tag}.h"], ops.gated_residual(x, T[f"{tag}.proj"], m[2]), 1.0, what=f"{tag} h")
         gemm_close(T[f"{tag}.up"], ops.fp8_linear(T[f"{tag}.hq"], T[f"{tag}.hs"], ws.up), f"{tag} up")
-        gemm_close(T[f"{tag}.down"], ops.fp8_linear(T[f"{tag}.gq"], T[f"{tag}.gs"], ws.down), f"{tag} down")
-        assert_ulp_close(T[f"{tag}.out"], ops.gated_residual(T[f"{tag}.h"], T[f"{tag}.down"], m[5]), 1.0,
-                         what=f"{tag} out")
+        out_ref = ops.fp8_scaled_mm_gated_residual(T[f"{tag}.gq"], ws.down.wq, T[f"{tag}.gs"], ws.down.ws,
+                                                   ws.down.bias, T[f"{tag}.h"], m[5])
+        gemm_close(T[f"{tag}.out"], out_ref, f"{tag} down + gated residual")
     q_img, k_img, v_img = ops.qkv_norm_rope_pack(T["img.qkv"], heads, W.img.q_norm, W.img.k_norm, cos, sin, 1e-6,
                                                  head_major=False)
     q_txt, k_txt, v_txt = ops.qkv_text_pack(T["txt.qkv"], heads, W.txt.q_norm, W.txt.k_norm, 1e-6)

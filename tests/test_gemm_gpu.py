@@ -10,7 +10,7 @@ matrix against torch._scaled_mm on the GPU.
 import pytest
 import torch
 
-from conftest import assert_guard_intact, guarded_empty
+from conftest import assert_guard_intact, assert_ulp_close, guarded_empty
 from oracle import ops
 
 pytestmark = pytest.mark.gpu
@@ -122,3 +122,45 @@ def test_gemm_rejects(jo, dev, cabi):
         jo.fp8_scaled_mm(a, b, s, s, torch.bfloat16, None)
     st = cabi.status_of("jo_fp8_scaled_mm", 0, 64, 0, 32, 0, 32, 0, 0, None, 64, 64, 32, cabi.JO_BF16, None)
     assert st == cabi.JO_ERR_INVALID
+
+
+@pytest.mark.parametrize("M,N,K,bias", [(10800, 3072, 12288, True), (200, 264, 512, False), (100, 512, 256, True),
+                                        (512, 3072, 12288, True)])
+def test_gemm_gated_residual(jo, dev, M, N, K, bias):
+    """Down projection + gated residual in the GEMM epilogue (dit.py:536-538)."""
+    aq, sa, bq, sb = operands(M, N, K, 11)
+    g = torch.Generator().manual_seed(12)
+    b = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16) if bias else None
+    res = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    gate = (0.1 * torch.randn(1, N, generator=g)).to(torch.bfloat16)
+    d = jo.fp8_scaled_mm_gated_residual(aq.to(dev), bq.to(dev), sa.to(dev), sb.to(dev), torch.bfloat16,
+                                        None if b is None else b.to(dev), res.to(dev), gate.to(dev))
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(13))[:160]
+    rows = torch.cat([rows, torch.tensor([0, M - 1])])
+    ref = ops.fp8_scaled_mm_gated_residual(aq[rows], bq, sa[rows], sb, b, res[rows], gate)
+    # the product enters in fp32 (no intermediate rounding): per element <= 2 ulp of the
+    # result plus |gate| * 2^-12 * rms(product) for the GEMM's accumulation order
+    prod = ops.fp8_scaled_mm(aq[rows], bq, sa[rows], sb, b, torch.float32)
+    atol = gate.float().abs().reshape(1, -1) * prod.pow(2).mean().sqrt() * 2.0 ** -12
+    assert_ulp_close(d.cpu()[rows], ref, 2.0, what="gated residual GEMM", atol=atol.expand_as(ref))
+    # against the unfused chain: GEMM rounded to bf16, then addcmul
+    unfused = ops.gated_residual(res[rows], ops.fp8_scaled_mm(aq[rows], bq, sa[rows], sb, b, torch.bfloat16), gate)
+    rel = ((d.cpu()[rows].float() - unfused.float()).norm() / unfused.float().norm()).item()
+    assert rel < 1e-3
+
+
+def test_gemm_gated_residual_in_place(jo, dev):
+    """D may alias the residual (same rows and stride)."""
+    from joyomni_ops import cabi
+
+    M, N, K = 300, 512, 256
+    aq, sa, bq, sb = operands(M, N, K, 14)
+    res = torch.randn(M, N, generator=torch.Generator().manual_seed(15)).to(torch.bfloat16)
+    gate = torch.full((N,), 0.5).to(torch.bfloat16)
+    ref = ops.fp8_scaled_mm_gated_residual(aq, bq, sa, sb, None, res, gate)
+    ag, bg, sag, sbg, rg, gg = aq.to(dev), bq.to(dev), sa.to(dev), sb.to(dev), res.to(dev), gate.to(dev)
+    cabi.call("jo_fp8_scaled_mm_gated_residual", rg.data_ptr(), N, ag.data_ptr(), K, bg.data_ptr(), bg.stride(1),
+              sag.data_ptr(), sbg.data_ptr(), 0, rg.data_ptr(), N, gg.data_ptr(), M, N, K, cabi.JO_BF16,
+              cabi.stream())
+    torch.cuda.synchronize()
+    assert_ulp_close(rg.cpu(), ref, 2.0, what="in place", atol=torch.full((M, N), 2.0 ** -10))
