@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
 // output ulp); the regrouped products move the fp32 result by a few fp32 ulps
 // (at most one bf16 ulp after rounding).
 constexpr int kQkWarps = 16;
-constexpr int kQkSlots = 2;
+constexpr int kQkSlots = 1;  // one 6 KB unit in flight per warp (measured faster than two)
 constexpr int kQkMaxIt = 16;  // head iterations held in registers (H <= 16 * 32/(D/8))
 
 __device__ __forceinline__ float2 bf2f(uint32_t w) {
