@@ -302,7 +302,7 @@ class Gemm(Workload):
 class Temb(Workload):
     """Timestep conditioning MLP at the model's shape (batch 1): sinusoid(256) -> linear_1
     (3072x256) -> SiLU -> linear_2 (3072x3072) -> SiLU -> time_proj (18432x3072); bound by
-    the 133 MB weight read (dit.py:574-579, 605-620, §8f rank 4)."""
+    the 133 MB weight read (dit.py:574-579, 605-620)."""
 
     name = "temb"
     desc = "timestep MLP: sinusoid(256) -> 3072 -> 3072 -> 18432, batch 1 (dit.py:574-620)"

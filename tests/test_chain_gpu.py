@@ -1,4 +1,4 @@
-"""GPU parity of the per-block chain and the fused ops it adds.
+"""GPU parity of the per-block chain (benchmark config 4) and the fused ops it adds.
 
 Stage by stage, each op of joyomni_ops.chain.block_forward is checked against the
 oracle applied to the GPU's own inputs of that stage (the per-op tolerances of

@@ -64,7 +64,7 @@ def test_gemm_bias(jo, dev, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(10800, 9216, 3072), (10800, 12288, 3072), (4096, 4096, 4096)])
 def test_gemm_baseline_shapes(jo, dev, M, N, K):
-    """BASELINE configs[3] (QKV and MLP-up projections) and the reference bench shape."""
+    """Benchmark config 3 (QKV and MLP-up projections) and the reference bench shape."""
     aq, sa, bq, sb = operands(M, N, K, 7)
     ag, bg, sag, sbg = aq.to(dev), bq.to(dev), sa.to(dev), sb.to(dev)
     d = jo.fp8_scaled_mm(ag, bg, sag, sbg, torch.bfloat16, None)

@@ -26,7 +26,7 @@ def chunk_tables(frames, h, w, t0, dims):
 
 @pytest.mark.parametrize("head_major", [True, False])
 def test_qkv_pack_config1(jo, dev, head_major):
-    """qkv [10800, 9216], 24 x 128 heads, 3x45x80 grid, t0 in [0, 64)."""
+    """Benchmark config 1: qkv [10800, 9216], 24 x 128 heads, 3x45x80 grid, t0 in [0, 64)."""
     L, H, D = 10800, 24, 128
     t0 = int(torch.randint(0, 64, (1,), generator=torch.Generator().manual_seed(7)).item())
     qkv = rand((L, 3 * H * D), 1)
