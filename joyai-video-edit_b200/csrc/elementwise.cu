@@ -32,6 +32,8 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads)
     gelu_vec_kernel(T* __restrict__ out, const T* __restrict__ x, int64_t nvec) {
   constexpr int V = Elt<T>::kVec;
+  pdl_wait();  // launched with launch_pdl: inputs complete from here on
+  pdl_trigger();
   const int64_t stride = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec;
        base += stride) {
@@ -68,6 +70,8 @@ __global__ void __launch_bounds__(kThreads)
     silu_mul_vec_kernel(T* __restrict__ out, int64_t os, const T* __restrict__ a, int64_t as,
                         const T* __restrict__ b, int64_t bs, int64_t rows, int64_t vpr) {
   constexpr int V = Elt<T>::kVec;
+  pdl_wait();  // launched with launch_pdl: inputs complete from here on
+  pdl_trigger();
   const int64_t nvec = rows * vpr;
   const int64_t stride = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec;
@@ -147,7 +151,8 @@ int gelu_t(void* out, const void* x, int64_t n, cudaStream_t st, const DeviceInf
     const int64_t nvec = n / V;
     if (nvec > 0) {
       const int grid = grid_for(gelu_vec_kernel<T>, nvec, di);
-      gelu_vec_kernel<T><<<grid, kThreads, 0, st>>>(o, xi, nvec);
+      if (cudaError_t e = launch_pdl(gelu_vec_kernel<T>, dim3(grid), dim3(kThreads), 0, st, o, xi, nvec))
+        return fail(JO_ERR_CUDA, "gelu_tanh: launch failed: %s", cudaGetErrorString(e));
       if (int s = after_launch("gelu_vec_kernel")) return s;
     }
     done = nvec * V;
@@ -174,7 +179,9 @@ int silu_mul_t(void* out, int64_t os, const void* a, int64_t as, const void* b, 
   if (vec) {
     const int64_t vpr = cols / V;
     const int grid = grid_for(silu_mul_vec_kernel<T>, rows * vpr, di);
-    silu_mul_vec_kernel<T><<<grid, kThreads, 0, st>>>(o, os, pa, as, pb, bs, rows, vpr);
+    if (cudaError_t e = launch_pdl(silu_mul_vec_kernel<T>, dim3(grid), dim3(kThreads), 0, st, o, os, pa, as, pb, bs,
+                                   rows, vpr))
+      return fail(JO_ERR_CUDA, "silu_mul: launch failed: %s", cudaGetErrorString(e));
     return after_launch("silu_mul_vec_kernel");
   }
   const int grid = (int)std::min<int64_t>(cdiv(rows * cols, kThreads), (int64_t)di->sm_count * 8);

@@ -449,6 +449,8 @@ __global__ void __launch_bounds__(kP_Threads, 1)
   cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs (our operands) are complete from here on
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -690,13 +692,15 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   cfg.blockDim = dim3(kP_Threads, 1, 1);
   cfg.dynamicSmemBytes = kP_SmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, a) != cudaSuccess) return fail(JO_ERR_CUDA, "fp8_scaled_mm: pair launch failed");
   return after_launch("fp8_gemm_pair_kernel");
 }

@@ -248,6 +248,8 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
   if (threadIdx.x < kQkWarps * kQkSlots) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
+  pdl_wait();  // the previous kernel's outputs (our inputs) are complete from here on
+  pdl_trigger();
   const uint32_t bar0 = base + 8u * (uint32_t)(warp * kQkSlots);
   const uint32_t slot0 = base + 256u + (uint32_t)(warp * kQkSlots) * slot_bytes;
   auto unit_ptr = [&](int i, int64_t& tok, int& part) -> __nv_bfloat16* {
@@ -450,7 +452,9 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
   int64_t per = cdiv(ntok, di->sm_count);
   if (per < 2) per = 2;
   const int64_t grid = cdiv(ntok, per);
-  kern<<<(unsigned)grid, kQkWarps * 32, smem, st>>>(a, (int)per, slot_bytes, di->fault);
+  if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(kQkWarps * 32), smem, st, a, (int)per, slot_bytes,
+                                 di->fault))
+    return fail(JO_ERR_CUDA, "qk kernel: launch failed: %s", cudaGetErrorString(e));
   return after_launch("qk_staged_kernel");
 }
 

@@ -577,6 +577,8 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   if (threadIdx.x < NG * m) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
+  pdl_wait();  // the previous kernel's outputs (our inputs) are complete from here on
+  pdl_trigger();
 
   const uint32_t bar0 = base + 8u * (uint32_t)(grp * m);
   const uint32_t slot0 = base + cfg.data_off + (uint32_t)(grp * m) * cfg.slot_bytes;
@@ -838,7 +840,8 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   const int64_t min_rows = 2 * ng;  // at least two rows per group before adding CTAs
   if (grid * min_rows > a.rows) grid = cdiv(a.rows, min_rows);
   if (grid < 1) grid = 1;
-  kern<<<(unsigned)grid, cfg.warps * 32, smem, st>>>(a, cfg, di->fault);
+  if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(cfg.warps * 32), smem, st, a, cfg, di->fault))
+    return fail(JO_ERR_CUDA, "row kernel: launch failed: %s", cudaGetErrorString(e));
   return after_launch("row_staged_kernel");
 }
 

@@ -76,6 +76,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x < kWarps * m) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
+  pdl_wait();  // the previous layer's output (our input) is complete from here on
+  pdl_trigger();
   const uint32_t bar0 = base + 8u * (uint32_t)(warp * m);
   const uint32_t slot0 = base + cfg.data_off + (uint32_t)(warp * m) * cfg.slot_bytes;
   auto unit_rows = [&](int u) { return min(R, nrows - u * R); };
@@ -179,7 +181,8 @@ int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, siz
       return fail(JO_ERR_CUDA, "timestep_mlp: cannot reserve shared memory");
     attr = true;
   }
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(a, cfg, b0, di->fault);
+  if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), smem, st, a, cfg, b0, di->fault))
+    return fail(JO_ERR_CUDA, "timestep_mlp: launch failed: %s", cudaGetErrorString(e));
   return JO_OK;
 }
 
