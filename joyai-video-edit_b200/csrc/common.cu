@@ -46,6 +46,7 @@ int device_info(const DeviceInfo** out) {
   if (dev < 0 || dev >= kMaxDevices) return fail(JO_ERR_CUDA, "device index %d out of range", dev);
   std::call_once(g_info_once[dev], [dev]() {
     DeviceInfo& d = g_info[dev];
+    d.ordinal = dev;
     cudaError_t r = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
     if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -60,6 +61,19 @@ int device_info(const DeviceInfo** out) {
     return fail(JO_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
                 d.major, d.minor);
   *out = &d;
+  return JO_OK;
+}
+
+int reserve_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, const DeviceInfo* di,
+                 const char* what) {
+  const uint64_t bit = 1ull << di->ordinal;
+  if (done.load(std::memory_order_acquire) & bit) return JO_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(JO_ERR_CUDA, "%s: cannot reserve %d bytes of shared memory: %s", what, bytes, cudaGetErrorString(e));
+  }
+  done.fetch_or(bit, std::memory_order_acq_rel);
   return JO_OK;
 }
 

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "joyomni_b200.h"
 
 namespace jo {
@@ -18,12 +20,18 @@ int fail(int code, const char* fmt, ...);
 int after_launch(const char* what);
 // Per-device facts, cached on first use.  Returns JO_OK or an error status.
 struct DeviceInfo {
+  int ordinal;  // CUDA device index (< 64)
   int sm_count;
   int major, minor;
   int max_smem_optin;
   unsigned int* fault;  // device address of this device's fault counter
 };
 int device_info(const DeviceInfo** out);
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device,
+// once per device: the attribute is per device, so `done` (one per kernel, at
+// the call site) records the devices already set (bit = device ordinal).
+int reserve_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, const DeviceInfo* di,
+                 const char* what);
 // Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes.
 int occupancy(const void* kernel, int threads, size_t smem);
 

@@ -649,12 +649,8 @@ template <typename OutT, int kEpi>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st,
                 const DeviceInfo* di) {
   auto kern = fp8_gemm_kernel<OutT, kEpi>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
-      return fail(JO_ERR_CUDA, "fp8_scaled_mm: cannot reserve %d bytes of shared memory", kSmemBytes);
-    attr = true;
-  }
+  static std::atomic<uint64_t> reserved{0};
+  if (int s = reserve_smem((const void*)kern, kSmemBytes, reserved, di, "fp8_scaled_mm")) return s;
   const int tiles = a.tiles_m * a.tiles_n;
   const int grid = tiles < di->sm_count ? tiles : di->sm_count;
   kern<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, a);
@@ -663,12 +659,14 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a,
 
 // CTA-pair launch: clusters of (2,1,1), as many as can be resident at once.
 template <typename OutT, int kEpi>
-int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st) {
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& a, cudaStream_t st,
+                     const DeviceInfo* di) {
   auto kern = fp8_gemm_pair_kernel<OutT, kEpi>;
-  static int max_clusters = 0;
+  static std::atomic<uint64_t> reserved{0};
+  if (int s = reserve_smem((const void*)kern, kP_SmemBytes, reserved, di, "fp8_scaled_mm")) return s;
+  static std::atomic<int> resident[64];  // resident CTA pairs, per device (0 = not queried yet)
+  int max_clusters = resident[di->ordinal].load(std::memory_order_relaxed);
   if (!max_clusters) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kP_SmemBytes) != cudaSuccess)
-      return fail(JO_ERR_CUDA, "fp8_scaled_mm: cannot reserve %d bytes of shared memory", kP_SmemBytes);
     cudaLaunchConfig_t qc = {};
     qc.gridDim = dim3(2, 1, 1);
     qc.blockDim = dim3(kP_Threads, 1, 1);
@@ -684,6 +682,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
     if (cudaOccupancyMaxActiveClusters(&n, (const void*)kern, &qc) != cudaSuccess || n < 1)
       return fail(JO_ERR_CUDA, "fp8_scaled_mm: no resident CTA pair");
     max_clusters = n;
+    resident[di->ordinal].store(n, std::memory_order_relaxed);
   }
   const int tiles = a.tiles_m * a.tiles_n;
   const int clusters = tiles < max_clusters ? tiles : max_clusters;
@@ -715,8 +714,8 @@ template <int kEpi>
 int dispatch_gemm(bool pair, int out_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
                   cudaStream_t st, const DeviceInfo* di) {
   if (pair)
-    return out_dtype == JO_BF16 ? launch_gemm_pair<__nv_bfloat16, kEpi>(ma, mb, g, st)
-                                : launch_gemm_pair<__half, kEpi>(ma, mb, g, st);
+    return out_dtype == JO_BF16 ? launch_gemm_pair<__nv_bfloat16, kEpi>(ma, mb, g, st, di)
+                                : launch_gemm_pair<__half, kEpi>(ma, mb, g, st, di);
   return out_dtype == JO_BF16 ? launch_gemm<__nv_bfloat16, kEpi>(ma, mb, g, st, di)
                               : launch_gemm<__half, kEpi>(ma, mb, g, st, di);
 }

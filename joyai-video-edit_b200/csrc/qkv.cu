@@ -442,12 +442,8 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
   if (smem > 220 * 1024) return JO_OK;
   taken = true;
   auto kern = qk_staged_kernel<kD, kMode, kPre, kRope>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
-      return fail(JO_ERR_CUDA, "qk kernel: cannot reserve shared memory");
-    attr = true;
-  }
+  static std::atomic<uint64_t> reserved{0};
+  if (int s = reserve_smem((const void*)kern, 220 * 1024, reserved, di, "qk kernel")) return s;
   const int64_t ntok = (int64_t)a.total_rows / ((int64_t)kParts * a.heads);
   int64_t per = cdiv(ntok, di->sm_count);
   if (per < 2) per = 2;

@@ -830,12 +830,8 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   cfg.cache_off = (cfg.red_off + (uint32_t)(ng * 3 * kMaxG * 4) + 127u) & ~127u;
   cfg.data_off = cfg.cache_off + cache_bytes;
   const size_t smem = cfg.data_off + (size_t)ng * cfg.m * cfg.slot_bytes;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
-      return fail(JO_ERR_CUDA, "row kernel: cannot reserve shared memory");
-    attr = true;
-  }
+  static std::atomic<uint64_t> reserved{0};
+  if (int s = reserve_smem((const void*)kern, 220 * 1024, reserved, di, "row kernel")) return s;
   int64_t grid = di->sm_count;
   const int64_t min_rows = 2 * ng;  // at least two rows per group before adding CTAs
   if (grid * min_rows > a.rows) grid = cdiv(a.rows, min_rows);

@@ -175,12 +175,8 @@ template <int kB, bool kSinIn, bool kSilu>
 int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, size_t smem, cudaStream_t st,
                const DeviceInfo* di) {
   auto kern = temb_layer_kernel<kB, kSinIn, kSilu>;
-  static bool attr = false;  // one per kernel instantiation
-  if (!attr) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBudget) != cudaSuccess)
-      return fail(JO_ERR_CUDA, "timestep_mlp: cannot reserve shared memory");
-    attr = true;
-  }
+  static std::atomic<uint64_t> reserved{0};  // one per kernel instantiation
+  if (int s = reserve_smem((const void*)kern, (int)kBudget, reserved, di, "timestep_mlp")) return s;
   if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), smem, st, a, cfg, b0, di->fault))
     return fail(JO_ERR_CUDA, "timestep_mlp: launch failed: %s", cudaGetErrorString(e));
   return JO_OK;
