@@ -150,3 +150,48 @@ def test_timestep_embedding_known_values():
     # frequency 0 is exactly 1: entries are cos(t), sin(t)
     assert abs(e[1, 0].item() - torch.cos(torch.tensor(1.0)).item()) < 1e-7
     assert abs(e[2, 128].item() - torch.sin(torch.tensor(999.0)).item()) < 1e-6
+
+
+def test_oracle_timestep_mlp_composition():
+    """The timestep MLP restatement composes the modules of WanTimeTextImageEmbedding
+    (dit.py:574-579, 605-620) in order: Timesteps -> bf16 -> Linear -> SiLU -> Linear ->
+    SiLU -> Linear; checked against the same composition with torch.nn modules in fp32
+    (bf16 rounding of each materialised tensor is the only difference)."""
+    import torch.nn as nn
+
+    g = torch.Generator().manual_seed(0)
+    F_, D, P = 64, 96, 192
+    l1, l2, l3 = nn.Linear(F_, D), nn.Linear(D, D), nn.Linear(D, P)
+    for m in (l1, l2, l3):
+        with torch.no_grad():
+            m.weight.copy_(torch.randn(m.weight.shape, generator=g) / m.weight.shape[1] ** 0.5)
+            m.bias.copy_(0.1 * torch.randn(m.bias.shape, generator=g))
+    ws = [t.detach().to(torch.bfloat16) for t in (l1.weight, l1.bias, l2.weight, l2.bias, l3.weight, l3.bias)]
+    t = torch.tensor([0.0, 17.5, 999.0])
+    vec, s1, s2 = ops.timestep_mlp(t, *ws)
+    with torch.no_grad():
+        for m, i in ((l1, 0), (l2, 2), (l3, 4)):
+            m.weight.copy_(ws[i].float())
+            m.bias.copy_(ws[i + 1].float())
+        e = ops.timestep_embedding(t, F_).to(torch.bfloat16).float()
+        ref = l3(nn.functional.silu(l2(nn.functional.silu(l1(e)))))
+    rel = ((vec.float() - ref).norm() / ref.norm()).item()
+    assert vec.shape == (3, P) and s1.shape == (3, D) and s2.shape == (3, D)
+    assert rel < 2e-2, rel
+
+
+def test_oracle_gated_residual_gemm_matches_unfused():
+    """fp8_scaled_mm_gated_residual = residual + gate * (fp8_scaled_mm in fp32), i.e. the
+    unfused chain (GEMM, then torch.addcmul) without the intermediate rounding."""
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(33, 64, generator=g).to(torch.bfloat16)
+    w = (0.05 * torch.randn(48, 64, generator=g)).to(torch.bfloat16)
+    aq, sa = ops.per_token_quant_fp8(x)
+    bq, sb = ops.quantize_weight_per_channel(w)
+    res = torch.randn(33, 48, generator=g).to(torch.bfloat16)
+    gate = (0.1 * torch.randn(1, 48, generator=g)).to(torch.bfloat16)
+    fused = ops.fp8_scaled_mm_gated_residual(aq, bq, sa, sb, None, res, gate)
+    prod = ops.fp8_scaled_mm(aq, bq, sa, sb, None, torch.float32)
+    assert torch.equal(fused, (res.float() + gate.float() * prod).to(torch.bfloat16))
+    unfused = ops.gated_residual(res, prod.to(torch.bfloat16), gate)
+    assert (fused.float() - unfused.float()).abs().max().item() <= 2 * 2.0 ** -7 * res.float().abs().max().item()
