@@ -571,6 +571,28 @@ def time_graph(graph, world: int) -> float:
     return start.elapsed_time(end)
 
 
+def time_allgather(wl, st, world: int, rank: int, iters: int = 10) -> dict:
+    """The chain's K/V all-gather alone (the chunk's K and V rows, in place), every rank
+    taking part; CUDA events on the launching stream, max over ranks."""
+    bufs, chain = st["bufs"], st["chain"]
+    for _ in range(2):
+        chain.gather_chunk_kv(bufs, rank, wl.group)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        chain.gather_chunk_kv(bufs, rank, wl.group)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / iters, world)
+    total = 2 * wl.L * wl.D * 2  # K and V rows of the chunk, bf16
+    return {"us": round(ms * 1e3, 1), "bytes_received_per_rank": int(total * (world - 1) / world),
+            "bus_gbs": round(total * (world - 1) / world / (ms * 1e-3) / 1e9, 1),
+            "note": "in-place all_gather_into_tensor of the chunk's K and V (NCCL), alone; in the "
+                    "block it overlaps the text stream on a side stream"}
+
+
 def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
     """The reference's CPU path (oracle port of its PyTorch code) on the host cores."""
     torch.set_num_threads(os.cpu_count() or 1)
@@ -706,6 +728,7 @@ def run_ours(args, wl: Workload):
     e2e_ms, _ = time_device(lambda i: wl.e2e_step(sets[i % 2], *hosts[i % 2]), max(2, args.steps // 4), world)
     e2e_steps = max(2, args.steps // 4)
 
+    gather = time_allgather(wl, sets[0], world, rank) if isinstance(wl, Chain) and world > 1 else None
     ms = max_over_ranks(total_ms / args.steps, world)
     kern_ms = max_over_ranks(per_ms, world)
     e2e_step_ms = max_over_ranks(e2e_ms / e2e_steps, world)
@@ -762,6 +785,8 @@ def run_ours(args, wl: Workload):
         line["roofline"]["frac"] = round(line["achieved_tflops"] / line["roofline"]["peak"], 4)
         line["e2e"].update(value=round(e2e_step_ms * 1e3, 1), unit="us")
         line.pop("pct_of_8TBs")
+        if gather is not None:
+            line["allgather"] = gather
         line["cpu_baseline"] = {"value": None, "unit": "us", "cores": os.cpu_count(), "kind": "port",
                                 "sample": "not run: the block is ~10 TFLOP (attention over 54k keys), hours of "
                                           "host-CPU time; the per-op CPU baselines are in the per-op lines"}
