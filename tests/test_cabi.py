@@ -125,3 +125,37 @@ def test_fake_shapes(jo):
 
 def test_norm_type_mapping(jo):
     assert jo._norm_code("layer") == 0 and jo._norm_code("rms") == 1 and jo._norm_code("bogus") == -1
+
+
+def header_params():
+    """name -> list of C parameter types, from every JO_API declaration in include/*.h."""
+    out = {}
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", " ", h.read_text(), flags=re.S)
+        for m in re.finditer(r"JO_API\s+[\w\s\*]+?\b(jo_\w+)\s*\(([^)]*)\)\s*;", text):
+            params = [p.strip() for p in m.group(2).split(",") if p.strip()]
+            if params == ["void"]:
+                params = []
+            out[m.group(1)] = [re.sub(r"\s+\w+$", "", p).replace(" ", "") for p in params]
+    return out
+
+
+def ctype_kind(c_type):
+    if c_type.endswith("*"):
+        return "ptr"
+    return {"int64_t": "i64", "int": "i32", "float": "f32", "jo_view4": "view4", "uint32_t": "u32"}[c_type]
+
+
+def test_ctypes_argument_kinds_match_header(cabi):
+    """Every ctypes argtype list has the header's arity and kinds (catches ABI drift)."""
+    import ctypes as C
+
+    kind = {C.c_void_p: "ptr", C.c_int64: "i64", C.c_int32: "i32", C.c_int: "i32", C.c_float: "f32",
+            cabi.JoView4: "view4"}
+    decls = header_params()
+    assert set(decls) == set(cabi.SIGNATURES)
+    for name, c_params in decls.items():
+        got = [kind.get(t, "ptr" if isinstance(t, type) and issubclass(t, C._Pointer) else repr(t))
+               for t in cabi.SIGNATURES[name]]
+        want = [ctype_kind(p) for p in c_params]
+        assert got == want, f"{name}: ctypes {got} vs header {want}"
