@@ -32,6 +32,11 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+int launch_failed(cudaError_t e, const char* what) {
+  cudaGetLastError();
+  return fail(JO_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+}
+
 int after_launch(const char* what) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   cudaError_t e = cudaGetLastError();

@@ -18,6 +18,9 @@ namespace jo {
 int fail(int code, const char* fmt, ...);
 // Checks cudaGetLastError() after a launch; counts the launch.
 int after_launch(const char* what);
+// A launch call returned `e`: clear the runtime's pending error (so the next
+// call does not report it) and return JO_ERR_CUDA with the reason.
+int launch_failed(cudaError_t e, const char* what);
 // Per-device facts, cached on first use.  Returns JO_OK or an error status.
 struct DeviceInfo {
   int ordinal;  // CUDA device index (< 64)

@@ -152,7 +152,7 @@ int gelu_t(void* out, const void* x, int64_t n, cudaStream_t st, const DeviceInf
     if (nvec > 0) {
       const int grid = grid_for(gelu_vec_kernel<T>, nvec, di);
       if (cudaError_t e = launch_pdl(gelu_vec_kernel<T>, dim3(grid), dim3(kThreads), 0, st, o, xi, nvec))
-        return fail(JO_ERR_CUDA, "gelu_tanh: launch failed: %s", cudaGetErrorString(e));
+        return launch_failed(e, "gelu_tanh");
       if (int s = after_launch("gelu_vec_kernel")) return s;
     }
     done = nvec * V;
@@ -181,7 +181,7 @@ int silu_mul_t(void* out, int64_t os, const void* a, int64_t as, const void* b, 
     const int grid = grid_for(silu_mul_vec_kernel<T>, rows * vpr, di);
     if (cudaError_t e = launch_pdl(silu_mul_vec_kernel<T>, dim3(grid), dim3(kThreads), 0, st, o, os, pa, as, pb, bs,
                                    rows, vpr))
-      return fail(JO_ERR_CUDA, "silu_mul: launch failed: %s", cudaGetErrorString(e));
+      return launch_failed(e, "silu_mul");
     return after_launch("silu_mul_vec_kernel");
   }
   const int grid = (int)std::min<int64_t>(cdiv(rows * cols, kThreads), (int64_t)di->sm_count * 8);

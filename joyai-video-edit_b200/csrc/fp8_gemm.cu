@@ -700,7 +700,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, a) != cudaSuccess) return fail(JO_ERR_CUDA, "fp8_scaled_mm: pair launch failed");
+  if (cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, a)) return launch_failed(e, "fp8_scaled_mm");
   return after_launch("fp8_gemm_pair_kernel");
 }
 

@@ -450,7 +450,7 @@ int launch_qk_staged(const QkArgs& a, cudaStream_t st, const DeviceInfo* di, boo
   const int64_t grid = cdiv(ntok, per);
   if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(kQkWarps * 32), smem, st, a, (int)per, slot_bytes,
                                  di->fault))
-    return fail(JO_ERR_CUDA, "qk kernel: launch failed: %s", cudaGetErrorString(e));
+    return launch_failed(e, "qk kernel");
   return after_launch("qk_staged_kernel");
 }
 

@@ -837,7 +837,7 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   if (grid * min_rows > a.rows) grid = cdiv(a.rows, min_rows);
   if (grid < 1) grid = 1;
   if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(cfg.warps * 32), smem, st, a, cfg, di->fault))
-    return fail(JO_ERR_CUDA, "row kernel: launch failed: %s", cudaGetErrorString(e));
+    return launch_failed(e, "row kernel");
   return after_launch("row_staged_kernel");
 }
 

@@ -178,7 +178,7 @@ int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, siz
   static std::atomic<uint64_t> reserved{0};  // one per kernel instantiation
   if (int s = reserve_smem((const void*)kern, (int)kBudget, reserved, di, "timestep_mlp")) return s;
   if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(kThreads), smem, st, a, cfg, b0, di->fault))
-    return fail(JO_ERR_CUDA, "timestep_mlp: launch failed: %s", cudaGetErrorString(e));
+    return launch_failed(e, "timestep_mlp");
   return JO_OK;
 }
 
