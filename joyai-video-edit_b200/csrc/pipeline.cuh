@@ -29,17 +29,6 @@ __device__ __forceinline__ void mbar_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 // try_wait with a suspend-time hint: the thread sleeps (no issue slots) until
 // the phase completes or the hint elapses, instead of spinning.
 constexpr uint32_t kSuspendNs = 1000000;  // 1 ms
@@ -96,19 +85,5 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
   return v;
 }
-
-// Ring of kSlots shared-memory slots fed by one producer thread with bulk
-// copies and drained by consumer warps.  Unit i of this CTA lives in slot
-// i % kSlots during its phase (i / kSlots) & 1.
-struct Ring {
-  uint32_t data;  // slot 0 data (shared address)
-  uint32_t bars;  // full[kSlots] then empty[kSlots]
-  uint32_t slot_bytes;
-  int slots;
-  __device__ __forceinline__ uint32_t slot(int i) const { return data + (uint32_t)(i % slots) * slot_bytes; }
-  __device__ __forceinline__ uint32_t full(int i) const { return bars + 8u * (uint32_t)(i % slots); }
-  __device__ __forceinline__ uint32_t empty(int i) const { return bars + 8u * (uint32_t)(slots + i % slots); }
-  __device__ __forceinline__ uint32_t parity(int i) const { return (uint32_t)((i / slots) & 1); }
-};
 
 }  // namespace jo
