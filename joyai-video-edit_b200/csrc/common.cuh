@@ -65,16 +65,6 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-inline int dtype_size(int dt) {
-  switch (dt) {
-    case JO_F32: return 4;
-    case JO_F16: return 2;
-    case JO_BF16: return 2;
-    case JO_E4M3: return 1;
-    default: return 0;
-  }
-}
-
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
