@@ -142,6 +142,74 @@ def main(ref_root: Path) -> None:
     wq, ws = fp8._quantize_weight_per_channel(wt)
     cases["weight_quant"] = dict(w=wt, q=wq.contiguous().view(torch.uint8), q_stride=tuple(wq.stride()), s=ws)
 
+    # --- edge cases of the same reference functions -------------------------------
+    # fp16 and fp32 inputs of _torch_rmsnorm (the native op takes fp32/fp16/bf16)
+    for i, dt in enumerate((torch.float16, torch.float32)):
+        g = gen(120 + i)
+        x = torch.randn(6, 1000, generator=g).to(dt)
+        w = (1 + 0.02 * torch.randn(1000, generator=g)).to(dt)
+        cases[f"rmsnorm_{str(dt).split('.')[-1]}"] = dict(x=x, w=w, eps=1e-6, out=sgl._torch_rmsnorm(x, w, 1e-6))
+    # per-row modulation through the call site's non-native path
+    g = gen(210)
+    x = torch.randn(1, 5, 1024, generator=g).to(bf)
+    shift = (0.1 * torch.randn(1, 5, 1024, generator=g)).to(bf)
+    scale = (0.1 * torch.randn(1, 5, 1024, generator=g)).to(bf)
+    cases["layernorm_modulate_per_row"] = dict(
+        x=x, shift=shift, scale=scale, eps=1e-6,
+        out=sgl.fused_layernorm_modulate(x, shift=shift, scale=scale, eps=1e-6))
+    # per-batch gate (gate [B, D] broadcast over each item's tokens)
+    g = gen(310)
+    res = torch.randn(2, 3, 512, generator=g).to(bf)
+    xx = torch.randn(2, 3, 512, generator=g).to(bf)
+    gate = (0.1 * torch.randn(2, 512, generator=g)).to(bf)
+    cases["fused_add_gate_batched"] = dict(res=res, x=xx, gate=gate, out=sgl.fused_add_gate(res, xx, gate))
+    # RoPE tables at the largest start frame the streaming loop uses (t0 = 63)
+    F2, H2, W2, t02 = 1, 5, 7, 63
+    t = (torch.arange(F2).float() + t02).repeat_interleave(H2 * W2)
+    h = torch.arange(H2).float().repeat_interleave(W2).repeat(F2)
+    w_ = torch.arange(W2).float().repeat(F2 * H2)
+    cos_l, sin_l = [], []
+    for dim, pos in zip((44, 42, 42), (t, h, w_)):
+        c, s = rope.get_1d_rotary_pos_embed(dim, pos, theta=10000.0)
+        cos_l.append(c)
+        sin_l.append(s)
+    cf2, sf2 = torch.cat(cos_l, 1), torch.cat(sin_l, 1)
+    ch2, sh2 = sgl.prepare_fused_rope((cf2, sf2), head_dim=128, device=torch.device("cpu"))
+    cases["rope_tables_t63"] = dict(frames=F2, height=H2, width=W2, t0=t02, dims=(44, 42, 42), theta=10000.0,
+                                    cos_full=cf2, sin_full=sf2, cos_half=ch2, sin_half=sh2)
+    # joint pack without a cache (the first chunk of a stream)
+    g = gen(510)
+    img_qkv = torch.randn(1, 6, 3, 2, 128, generator=g).to(bf)
+    txt_qkv = torch.randn(1, 4, 3, 2, 128, generator=g).to(bf)
+    tqw = torch.randn(128, generator=g).to(bf)
+    tkw = torch.randn(128, generator=g).to(bf)
+    iq, ik, iv = img_qkv.unbind(2)
+    tq, tk, tv = txt_qkv.unbind(2)
+    oq, ok, ov = sgl.fused_joint_qkv_pack(iq, ik, iv, tq, tk, tv, None, None, tqw, tkw, 1e-6)
+    cases["joint_qkv_pack_nocache"] = dict(img_qkv=img_qkv, txt_qkv=txt_qkv, txt_q_weight=tqw, txt_k_weight=tkw,
+                                           eps=1e-6, out_q=oq, out_k=ok, out_v=ov)
+    # per-token quant: fp16 input, negative zeros, an all-tiny row (amax below the
+    # 1e-8 clamp), one dominant element (the rest in e4m3's subnormal range),
+    # values near the bf16 maximum, and one-signed rows
+    g = gen(710)
+    x = torch.randn(9, 256, generator=g)
+    x[0] = -0.0
+    x[1] *= 1e-10
+    x[2] *= 1e-3
+    x[2, 17] = 50.0
+    x[3] *= 1e36
+    x[4] = x[4].abs()
+    x[5] = -x[5].abs()
+    x[6, ::2] = 0.0
+    xb = x.to(bf)
+    qq, ss = fp8._quantize_per_token_impl(xb)
+    cases["per_token_quant_edges"] = dict(x=xb, q=qq.view(torch.uint8), s=ss)
+    xh = torch.randn(17, 512, generator=gen(711)).to(torch.float16)
+    xh[0] *= 2000.0  # |x| up to ~1e4, inside fp16's range
+    xh[1] = 0.0
+    qq, ss = fp8._quantize_per_token_impl(xh)
+    cases["per_token_quant_f16"] = dict(x=xh, q=qq.view(torch.uint8), s=ss)
+
     # --- GELU-tanh (the reference's own call) ------------------------------------
     g = gen(800)
     x = (torch.randn(6, 1024, generator=g) * torch.tensor([0.1, 1.0, 3.0, 6.0, 10.0, 30.0])[:, None]).to(bf)

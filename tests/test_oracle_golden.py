@@ -20,6 +20,13 @@ def test_rmsnorm_bit_exact(golden):
         assert torch.equal(out, c["out"]), name
 
 
+def test_rmsnorm_f16_f32_bit_exact(golden):
+    for name in ("rmsnorm_float16", "rmsnorm_float32"):
+        c = golden[name]
+        out = ops.rmsnorm(c["x"], c["w"], c["eps"])
+        assert out.dtype == c["out"].dtype and torch.equal(out, c["out"]), name
+
+
 def test_rmsnorm_model_vs_kernel_semantics(golden):
     # The model's double-rounding RMSNorm is within 1 ulp of the single-rounding one.
     c = golden["rmsnorm_7x3072"]
@@ -37,21 +44,37 @@ def test_layernorm_modulate(golden):
     assert_bf16_close(one, c["out"].reshape(-1, 3072), 4.0, floor=0.5, what="ln_mod single vs shim")
 
 
+def test_layernorm_modulate_per_row(golden):
+    c = golden["layernorm_modulate_per_row"]
+    assert torch.equal(ops.layernorm_modulate_shim(c["x"], c["shift"], c["scale"], c["eps"]), c["out"])
+    D = c["x"].shape[-1]
+    one = ops.norm_scale_shift(c["x"].reshape(-1, D), None, None, c["scale"].reshape(-1, D),
+                               c["shift"].reshape(-1, D), "layer", c["eps"])
+    assert_bf16_close(one, c["out"].reshape(-1, D), 4.0, floor=0.5, what="per-row ln_mod single vs shim")
+
+
 def test_gated_residual_bit_exact(golden):
     c = golden["fused_add_gate"]
     out = ops.gated_residual(c["res"], c["x"], c["gate"].unsqueeze(1))
     assert torch.equal(out, c["out"])
+    # gate [B, D] per batch item == a per-row [B*L, D] gate on the flattened rows
+    c = golden["fused_add_gate_batched"]
+    B, L, D = c["res"].shape
+    rows_gate = c["gate"][:, None, :].expand(B, L, D).reshape(-1, D)
+    out = ops.gated_residual(c["res"].reshape(-1, D), c["x"].reshape(-1, D), rows_gate)
+    assert torch.equal(out, c["out"].reshape(-1, D))
 
 
 def test_rope_tables_bit_exact(golden):
     from joyomni_ops import rope
 
-    c = golden["rope_tables"]
-    pos = rope.grid_positions(c["frames"], c["height"], c["width"], c["t0"])
-    cos, sin = rope.rope_3d(pos, c["dims"], c["theta"])
-    assert torch.equal(cos, c["cos_full"]) and torch.equal(sin, c["sin_full"])
-    ch, sh = rope.paired_tables(cos, sin)
-    assert torch.equal(ch, c["cos_half"]) and torch.equal(sh, c["sin_half"])
+    for name in ("rope_tables", "rope_tables_t63"):
+        c = golden[name]
+        pos = rope.grid_positions(c["frames"], c["height"], c["width"], c["t0"])
+        cos, sin = rope.rope_3d(pos, c["dims"], c["theta"])
+        assert torch.equal(cos, c["cos_full"]) and torch.equal(sin, c["sin_full"]), name
+        ch, sh = rope.paired_tables(cos, sin)
+        assert torch.equal(ch, c["cos_half"]) and torch.equal(sh, c["sin_half"]), name
 
 
 def test_qk_norm_rope(golden):
@@ -88,6 +111,21 @@ def test_joint_qkv_pack(golden):
     assert_bf16_close(ok, c["out_k"], 1.0, what="joint k")
 
 
+def test_joint_qkv_pack_without_cache(golden):
+    c = golden["joint_qkv_pack_nocache"]
+    iq, ik, iv = c["img_qkv"].unbind(2)
+    tq, tk, tv = c["txt_qkv"].unbind(2)
+    args = (iq, ik, iv, tq, tk, tv, None, None, c["txt_q_weight"], c["txt_k_weight"], c["eps"])
+    sq, sk, sv = ops.joint_qkv_pack_shim(*args)
+    assert torch.equal(sq, c["out_q"]) and torch.equal(sk, c["out_k"]) and torch.equal(sv, c["out_v"])
+    oq, ok, ov = ops.joint_qkv_pack(*args)
+    assert torch.equal(ov, c["out_v"])
+    n_img = iq.shape[1]
+    assert torch.equal(oq[:, :n_img], c["out_q"][:, :n_img]) and torch.equal(ok[:, :n_img], c["out_k"][:, :n_img])
+    assert_bf16_close(oq, c["out_q"], 1.0, what="joint q, no cache")
+    assert_bf16_close(ok, c["out_k"], 1.0, what="joint k, no cache")
+
+
 def test_cached_kv_rotation(golden):
     c = golden["cached_k_rotation"]
     L = c["cos"].shape[0]
@@ -104,9 +142,22 @@ def test_per_token_quant_bit_exact(golden):
     q, s = ops.per_token_quant_fp8(c["x"])
     assert torch.equal(q.view(torch.uint8), c["q"])
     assert torch.equal(s, c["s"])
-    # zero row: scale 1e-8/448, bytes 0 (the PyTorch path, not the CUDA kernel's 0)
-    assert s[0].item() == torch.tensor(1e-8, dtype=torch.float32).item() / 448.0 or s[0].item() > 0
+    # zero row: the amax clamp gives scale fp32(1e-8) / 448 (not the reference kernel's 0), bytes 0
+    assert torch.equal(s[0], torch.tensor([1e-8], dtype=torch.float32) / 448.0)
     assert (q[0].view(torch.uint8) == 0).all()
+
+
+def test_per_token_quant_edges_bit_exact(golden):
+    # negative zeros, amax below the 1e-8 clamp, e4m3 subnormals, |x| near the bf16
+    # maximum, one-signed rows, fp16 input
+    for name in ("per_token_quant_edges", "per_token_quant_f16"):
+        c = golden[name]
+        q, s = ops.per_token_quant_fp8(c["x"])
+        assert torch.equal(q.view(torch.uint8), c["q"]), name
+        assert torch.equal(s, c["s"]), name
+    c = golden["per_token_quant_edges"]
+    assert (c["q"][0] == 0x80).all()  # -0.0 keeps its sign through the e4m3 cast
+    assert (c["q"][1] != 0).any()  # values below the clamp are scaled up, not flushed
 
 
 def test_weight_quant_bit_exact(golden):
