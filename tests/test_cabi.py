@@ -58,6 +58,14 @@ def test_ctypes_binding_covers_header(cabi):
     assert header_symbols() == set(cabi.SIGNATURES), "cabi.SIGNATURES out of sync with include/*.h"
 
 
+def test_integration_table_covers_header():
+    # the maintainer-facing table of entry points names every declared symbol
+    text = (REPO / "INTEGRATION.md").read_text()
+    section = text.split("## 4. Entry points of the C ABI", 1)[1].split("\n## ", 1)[0]
+    listed = set(re.findall(r"`(jo_\w+)`", section))
+    assert header_symbols() == listed, f"INTEGRATION.md table out of sync: {header_symbols() ^ listed}"
+
+
 def test_abi_info(cabi):
     L = cabi.lib()
     assert L.jo_abi_version() == 1
