@@ -25,6 +25,9 @@ namespace {
   JO_CHECK_DTYPE(x, dt)
 
 void jo_check(int status, const char* op) {
+  // An unsupported device raises NotImplementedError, as the reference's GEMM does on an
+  // architecture it has no kernel for (fp8_gemm.cu:1531); every other failure is a RuntimeError.
+  TORCH_CHECK_NOT_IMPLEMENTED(status != JO_ERR_UNSUPPORTED, "joyomni_ops::", op, ": ", jo_last_error());
   TORCH_CHECK(status == JO_OK, "joyomni_ops::", op, " failed (", jo_status_name(status), "): ",
               jo_last_error());
 }
