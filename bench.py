@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 joyomni_ops hot path (one JSON line on rank 0).
 
-Default workload: the fused QKV pack + per-head
+Headline workload: the fused QKV pack + per-head
 q/k RMSNorm + 3D RoPE, qkv bf16 [10800, 9216] (3 latent frames x 45x80 tokens,
 24 heads x 128) -> q/k/v bf16 [24, 10800, 128], RoPE theta 10000 split 44/42/42
 on the (t, h, w) grid with a random chunk start t0 in [0, 64).  One step = one
@@ -9,13 +9,17 @@ pass of the op over one chunk.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload qkv_pack|rmsnorm|ln_mod|gated_ln|gelu|silu_mul|quant|rmsnorm_quant|
-                                gemm_qkv|gemm_up|temb|chain]
+                                gemm_qkv|gemm_up|temb|chain] [--no-per-op] [--no-chain]
 
-N > 1 runs under torchrun, one process per GPU; every rank processes its own
-chunk (independent token partitions: weak scaling, no collective on the data
-path); time is the max over ranks of CUDA-event time.  ``--impl reference``
-times the reference's CPU implementation of the same path (the oracle port of
-its PyTorch code) on the host cores, on rank 0 only.
+The default line also carries ``per_op`` (every other BASELINE config at 1 GPU,
+each with its roofline fraction and a short CPU baseline) and ``chain`` (the
+per-block op chain of configs[4]; sequence parallel over the N GPUs with the
+NCCL all-gather of the chunk's K/V).  N > 1 runs under torchrun, one process per
+GPU; for the headline every rank processes its own chunk (independent token
+partitions: weak scaling, no collective on its data path); time is the max over
+ranks of CUDA-event time.  ``--impl reference`` times the reference's CPU
+implementation of the headline (its PyTorch fallback sequence, restated by the
+oracle) on the host cores, on rank 0 only; it never imports this package.
 """
 from __future__ import annotations
 
@@ -73,6 +77,10 @@ class Workload:
     def algo_bytes(self) -> int:
         raise NotImplementedError
 
+    def config(self) -> dict:
+        """The workload as both arms of the benchmark name it (identical dicts)."""
+        return {"workload": self.desc, **self.shape}
+
     def make(self, dev, seed: int):
         raise NotImplementedError
 
@@ -105,21 +113,31 @@ class QkvPack(Workload):
         L, H, D = self.L, self.H, self.D
         return L * 3 * H * D * 2 * 2 + 2 * L * (D // 2) * 2  # qkv read + q/k/v written + cos/sin read
 
-    def _inputs(self, seed, dev):
-        from joyomni_ops import rope
-
+    def _inputs(self, seed, dev, tables):
         g = torch.Generator().manual_seed(seed)
         t0 = int(torch.randint(0, 64, (1,), generator=g).item())
         qkv = torch.randn(self.L, 3 * self.H * self.D, generator=g).to(BF)
         qw = (1 + 0.02 * torch.randn(self.D, generator=g)).to(BF)
         kw = (1 + 0.02 * torch.randn(self.D, generator=g)).to(BF)
-        cos, sin = rope.video_chunk_tables(3, 45, 80, t0, dims=(44, 42, 42))
+        cos, sin = tables(t0)
         return dict(qkv=qkv.to(dev), qw=qw.to(dev), kw=kw.to(dev), cos=cos.to(dev), sin=sin.to(dev))
+
+    @staticmethod
+    def _product_tables(t0):
+        from joyomni_ops import rope
+
+        return rope.video_chunk_tables(3, 45, 80, t0, dims=(44, 42, 42))
+
+    @staticmethod
+    def _oracle_tables(t0):
+        from oracle import ops  # the CPU arm builds its tables without this package
+
+        return ops.rope_video_tables(3, 45, 80, t0, (44, 42, 42))[1]
 
     def make(self, dev, seed):
         import joyomni_ops as jo
 
-        x = self._inputs(seed, dev)
+        x = self._inputs(seed, dev, self._product_tables)
         q, k, v = jo.qkv_norm_rope_pack(x["qkv"], self.H, x["qw"], x["kw"], x["cos"], x["sin"], 1e-6, True)
         return dict(inputs={"qkv": x["qkv"]}, outputs={"q": q, "k": k, "v": v}, x=x, jo=jo)
 
@@ -127,21 +145,23 @@ class QkvPack(Workload):
         x = st["x"]
         return st["jo"].qkv_norm_rope_pack(x["qkv"], self.H, x["qw"], x["kw"], x["cos"], x["sin"], 1e-6, True)
 
+    CHUNK_TOKENS = 1350  # 8 chunks of the 10800 tokens for the pipelined host path
+
     def e2e_step(self, st, host_in, host_out):
+        # the public host-buffer op: uploads, packs and downloads overlap chunk by chunk
         x = st["x"]
-        x["qkv"].copy_(host_in["qkv"], non_blocking=True)
-        q, k, v = self.step(st)
-        host_out["q"].copy_(q, non_blocking=True)
-        host_out["k"].copy_(k, non_blocking=True)
-        host_out["v"].copy_(v, non_blocking=True)
+        st["jo"].qkv_norm_rope_pack_host(host_in["qkv"], self.H, x["qw"], x["kw"], x["cos"], x["sin"], host_out["q"],
+                                         host_out["k"], host_out["v"], 1e-6, True, self.CHUNK_TOKENS)
 
     def make_cpu(self, seed):
-        return self._inputs(seed, "cpu")
+        return self._inputs(seed, "cpu", self._oracle_tables)
 
     def cpu_step(self, x):
+        # the reference's own sequence without its native ops: strided q/k, _torch_rmsnorm -> bf16,
+        # full-width rotation -> bf16 (sgl_fused_ops.py:170-199), q/k/v materialised head-major
         from oracle import ops
 
-        return ops.qkv_norm_rope_pack(x["qkv"], self.H, x["qw"], x["kw"], x["cos"], x["sin"], 1e-6, True)
+        return ops.qkv_pack_reference_path(x["qkv"], self.H, x["qw"], x["kw"], x["cos"], x["sin"], 1e-6)
 
 
 class RowOp(Workload):
@@ -255,8 +275,6 @@ class Gemm(Workload):
         return self.M * self.K + self.K * self.N + 2 * self.M * self.N + 4 * (self.M + self.N)
 
     def _inputs(self, seed, dev):
-        from oracle import ops  # noqa: F401  (operand preparation only; never the timed path)
-
         g = torch.Generator().manual_seed(seed)
         x = torch.randn(self.M, self.K, generator=g).to(BF)
         w = (0.02 * torch.randn(self.N, self.K, generator=g)).to(BF)
@@ -395,7 +413,8 @@ class Chain(Workload):
 
     def step(self, st):
         return st["chain"].block_forward(st["img"], st["txt"], st["vec"], st["cos"], st["sin"], st["w"], st["bufs"],
-                                         group=self.group, rank=self.rank, side_stream=st["side"])
+                                         group=self.group, rank=self.rank, side_stream=st["side"],
+                                         events=st.get("events"))
 
     def e2e_step(self, st, host_in, host_out):
         st["img"].copy_(host_in["img"], non_blocking=True)
@@ -594,7 +613,7 @@ def time_allgather(wl, st, world: int, rank: int, iters: int = 10) -> dict:
 
 
 def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
-    """The reference's CPU path (oracle port of its PyTorch code) on the host cores."""
+    """The reference's CPU path (oracle restatement of its PyTorch code) on the host cores."""
     torch.set_num_threads(os.cpu_count() or 1)
     x = wl.make_cpu(seed=1)
     wl.cpu_step(x)  # warm-up
@@ -605,13 +624,19 @@ def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
         el = time.perf_counter() - t0
         if el >= min_seconds or n >= 200:
             break
-    return {"value": round(wl.algo_bytes() * n / el / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
-            "kind": "port",
+    thr = torch.get_num_threads()
+    if isinstance(wl, Gemm):
+        return {"value": round(2 * x["rows"] * wl.N * wl.K * n / el / 1e12, 5), "unit": "TFLOP/s", "cores": thr,
+                "kind": "port", "sample": f"{n} x {x['rows']} rows of A against the full B, fp32 dequantised "
+                                          f"GEMM (fp8_linear.py fallback math), {el:.1f} s, {thr} threads"}
+    return {"value": round(wl.algo_bytes() * n / el / 1e9, 3), "unit": "GB/s", "cores": thr, "kind": "port",
             "sample": f"{n} full passes of the workload ({wl.algo_bytes() / 1e6:.1f} MB each) in {el:.1f} s, "
-                      f"torch CPU restatement of the reference PyTorch path, {torch.get_num_threads()} threads"}
+                      f"torch CPU restatement of the reference PyTorch path, {thr} threads"}
 
 
 def run_reference(args, wl: Workload):
+    """The reference arm: the reference's own CPU sequence for the headline workload, on the
+    host cores, through the oracle restatement only (this package is never imported)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # rank 0 alone times the CPU reference; other ranks exit without work
@@ -630,189 +655,213 @@ def run_reference(args, wl: Workload):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": wl.desc, **wl.shape},
+        "config": wl.config(),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": "each step one full pass of the workload on the host CPU (torch restatement of "
-                                   "the reference's PyTorch path)"},
+                         "sample": "each step one full pass of the workload on the host CPU: the reference's "
+                                   "PyTorch fallback sequence (rearrange, _torch_rmsnorm -> bf16, full-width "
+                                   "rotation -> bf16; sgl_fused_ops.py:170-199) restated by oracle/ops.py and "
+                                   "pinned bit-exactly to the reference's own code by tests/golden"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, wl: Workload):
-    world, rank, local = dist_init(args.gpus)
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+def graph_time(wl: Workload, dev, steps: int, warmup: int, world: int, rank: int, seed0: int):
+    """K steps of wl captured in one CUDA graph over rotating buffer sets (>= 2x L2 in total);
+    returns (sets, graph, launches, nsets) ready for timed replays."""
     from joyomni_ops import cabi
 
-    if isinstance(wl, Chain):
-        import torch.distributed as dist
-
-        wl.world, wl.rank = world, rank
-        wl.group = dist.group.WORLD if world > 1 else None
-
-    # rotating buffer sets (inputs, and the outputs each step allocates, kept
-    # alive until their set comes round again): the rotating footprint is at
-    # least twice the 126 MB L2, so no step reads or overwrites what the
-    # previous ones left in L2 (the block chain's working set is ~2 GB by
-    # itself: one set)
-    if isinstance(wl, Chain):
-        nsets = 1
-    else:
-        nsets = max(2, min(16, -(-2 * L2_BYTES // wl.algo_bytes())))
-    sets = [wl.make(dev, seed=1 + rank * 16 + i) for i in range(nsets)]
+    nsets = max(2, min(16, -(-2 * L2_BYTES // max(1, wl.algo_bytes()))))
+    sets = [wl.make(dev, seed=seed0 + rank * 16 + i) for i in range(nsets)]
     ring = [None] * nsets
 
     def step(i):
         ring[i % nsets] = wl.step(sets[i % nsets])
 
     torch.cuda.synchronize()
-    for i in range(max(args.warmup, 3)):
+    for i in range(max(warmup, 3)):
         step(i)
     torch.cuda.synchronize()
-
-    # the timed K steps run as one CUDA graph replay (no host launch gaps between
-    # the kernels); the block chain, which carries NCCL collectives and library
-    # attention, runs eagerly
-    graph = None
-    if not isinstance(wl, Chain):
-        l0 = cabi.launch_count()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for i in range(args.steps):
-                step(i)
-        launches = cabi.launch_count() - l0  # kernels per replay
-        graph.replay()
-        torch.cuda.synchronize()
-
-    clocks = ClockSampler(local) if rank == 0 else None
-    if clocks:
-        clocks.start()
-    # soak so the clock record covers >= ~1 s of this workload around the timed region;
-    # every rank runs the same number of soak iterations (the chain's steps carry
-    # collectives), agreed as the max over ranks of each rank's own estimate
-    def soak_iter(i):
-        if graph is not None:
-            graph.replay()
-        else:
+    l0 = cabi.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
             step(i)
+    launches = cabi.launch_count() - l0
+    graph.replay()
+    torch.cuda.synchronize()
+    return sets, ring, graph, launches, nsets
 
+
+def soak(fn, world, seconds=1.0):
+    """Run fn until ~seconds of device work have passed (every rank the same count), so the
+    clock record around the timed region reflects this workload."""
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(2):
-        soak_iter(i)
+        fn(i)
     torch.cuda.synchronize()
     per_iter = max((time.perf_counter() - t0) / 2, 1e-6)
-    n_soak = int(max_over_ranks(float(min(4096, int(1.0 / per_iter) + 1)), world))
-    for i in range(n_soak):
-        soak_iter(i)
+    n = int(max_over_ranks(float(min(4096, int(seconds / per_iter) + 1)), world))
+    for i in range(n):
+        fn(i)
         if i % 16 == 15:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
-    if graph is not None:
-        total_ms = time_graph(graph, world)
-        per_ms = total_ms / args.steps
-    else:
-        l0 = cabi.launch_count()
-        total_ms, per_ms = time_device(step, args.steps, world)
-        launches = cabi.launch_count() - l0
+
+
+def run_headline(args, wl: Workload, world: int, rank: int, local: int, dev):
+    sets, ring, graph, launches, nsets = graph_time(wl, dev, args.steps, args.warmup, world, rank, 1)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    soak(lambda i: graph.replay(), world)
+    total_ms = time_graph(graph, world)
     clk = clocks.stop() if clocks else None
     del graph
-    sets = sets[:2] if len(sets) >= 2 else sets * 2
-
+    per_ms = total_ms / args.steps
+    two = sets[:2]
     # end to end through the public op with host (pinned) buffers
-    hosts = [wl.make_host(s) for s in sets]
+    hosts = [wl.make_host(s) for s in two]
     for i in range(2):
-        wl.e2e_step(sets[i], *hosts[i])
+        wl.e2e_step(two[i], *hosts[i])
     torch.cuda.synchronize()
-    e2e_ms, _ = time_device(lambda i: wl.e2e_step(sets[i % 2], *hosts[i % 2]), max(2, args.steps // 4), world)
     e2e_steps = max(2, args.steps // 4)
-
-    gather = time_allgather(wl, sets[0], world, rank) if isinstance(wl, Chain) and world > 1 else None
-    ms = max_over_ranks(total_ms / args.steps, world)
-    kern_ms = max_over_ranks(per_ms, world)
+    e2e_ms, _ = time_device(lambda i: wl.e2e_step(two[i % 2], *hosts[i % 2]), e2e_steps, world)
+    ms = max_over_ranks(per_ms, world)
     e2e_step_ms = max_over_ranks(e2e_ms / e2e_steps, world)
-    if rank != 0:
-        _finish(world)
-        return
     B = wl.algo_bytes()
     value = world * B / (ms * 1e-3) / 1e9
-    achieved = B / (kern_ms * 1e-3) / 1e9
     peak, peak_kind = measured_hbm_gbs()
-    traffic = profile_traffic(wl.name)
-    if isinstance(wl, Gemm):
-        fp8_peak = measure_fp8_peak(dev)
-        tflops = wl.flops() / (kern_ms * 1e-3) / 1e12
-        line_tensor = {"bound": "tensor", "achieved": round(tflops, 1), "peak": round(fp8_peak, 1),
-                       "unit": "TFLOP/s", "frac": round(tflops / fp8_peak, 4),
-                       "peak_source": "measured in this run: cuBLASLt FP8 torch._scaled_mm 8192^3, best of 1 s",
-                       "nominal_dense_fp8": 4500.0, "traffic": traffic, "kernel_us": round(kern_ms * 1e3, 2)}
     h2d = sum(t.numel() * t.element_size() for t in hosts[0][0].values())
     d2h = sum(t.numel() * t.element_size() for t in hosts[0][1].values())
-    line = {
+    del sets, ring, hosts, two
+    torch.cuda.empty_cache()
+    achieved = B / (ms * 1e-3) / 1e9
+    return {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "pct_of_8TBs": round(100.0 * value / world / NOMINAL_HBM_GBS, 2),
-        "config": {"workload": wl.desc, **wl.shape, "algo_bytes_per_step": B,
+        "config": wl.config(),
+        "timing": {"algo_bytes_per_step": B,
                    "l2": f"{nsets} rotating buffer sets of inputs + outputs, >= 2x the 126 MB L2 in total",
-                   "timing": "K steps captured in one CUDA graph, one replay timed with CUDA events"
-                   if not isinstance(wl, Chain) else "K eager steps, CUDA events",
+                   "method": "K steps captured in one CUDA graph, one replay timed with CUDA events, max over ranks",
                    "parallelism": f"{world} independent token partitions (one chunk per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": traffic, "kernel_us": round(kern_ms * 1e3, 2)},
+                     "traffic": profile_traffic(wl.name), "kernel_us": round(ms * 1e3, 2)},
         "e2e": {"value": round(world * B / (e2e_step_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_step_ms, 3),
-                "api": "torch.ops.joyomni_ops (pinned host buffers, copies inside the timed region)"},
+                "api": "torch.ops.joyomni_ops.qkv_norm_rope_pack_host (C ABI jo_qkv_norm_rope_pack_host): pinned "
+                       "host buffers, uploads / pack / downloads overlapped by token chunks, all copies inside the "
+                       "timed region"},
         "gpu_launches": int(launches),
         "clocks": clk,
     }
+
+
+PER_OP = ["rmsnorm", "ln_mod", "gated_ln", "gelu", "silu_mul", "quant", "rmsnorm_quant", "gemm_qkv", "gemm_up",
+          "temb"]
+
+
+def run_per_op(args, dev, local: int) -> dict:
+    """Every other BASELINE config at 1 GPU, timed like the headline (graph replay over
+    rotating buffers, best of 3 replays), each with its roofline fraction and a short CPU
+    baseline of the reference's PyTorch path."""
+    peak, peak_kind = measured_hbm_gbs()
+    fp8_peak = measure_fp8_peak(dev)
+    out = {"_peaks": {"hbm_gbs": peak, "hbm_source": f"{peak_kind} (MEASURED_PEAKS.json)",
+                      "fp8_tflops": round(fp8_peak, 1),
+                      "fp8_source": "cuBLASLt FP8 (torch._scaled_mm 8192^3, row/col scales) in this run, best of 1 s"}}
+    clocks = ClockSampler(local)
+    clocks.start()
+    for name in PER_OP:
+        wl = workloads()[name]
+        sets, ring, graph, launches, nsets = graph_time(wl, dev, args.steps, args.warmup, 1, 0, 101)
+        best = float("inf")
+        for _ in range(3):
+            best = min(best, time_graph(graph, 1) / args.steps)
+        del graph, sets, ring
+        torch.cuda.empty_cache()
+        rec = {"config": wl.config(), "us": round(best * 1e3, 2), "launches_per_step": launches / args.steps}
+        if isinstance(wl, Gemm):
+            tf = wl.flops() / (best * 1e-3) / 1e12
+            rec.update(tflops=round(tf, 1), frac=round(tf / fp8_peak, 4), bound="tensor (FP8)",
+                       frac_of_nominal_4500=round(tf / 4500.0, 4))
+        else:
+            gbs = wl.algo_bytes() / (best * 1e-3) / 1e9
+            rec.update(algo_bytes=wl.algo_bytes(), gbs=round(gbs, 1), frac=round(gbs / peak, 4), bound="hbm",
+                       pct_of_8TBs=round(100 * gbs / NOMINAL_HBM_GBS, 2))
+        out[name] = rec
+    out["_clocks"] = clocks.stop()
+    if not args.no_cpu_baseline:
+        for name in PER_OP:
+            out[name]["cpu_baseline"] = cpu_baseline(workloads()[name], min_seconds=1.5)
+    return out
+
+
+def run_chain(args, world: int, rank: int, dev) -> dict:
+    """one double-stream block for one chunk, sequence parallel over the ranks."""
+    import torch.distributed as dist
+
+    wl = workloads()["chain"]
+    wl.world, wl.rank = world, rank
+    wl.group = dist.group.WORLD if world > 1 else None
+    st = wl.make(dev, seed=1)
+    for _ in range(max(args.warmup, 3)):
+        wl.step(st)
+    torch.cuda.synchronize()
+    steps = max(5, args.steps // 2)
+    total_ms, per_ms = time_device(lambda i: wl.step(st), steps, world)
+    ms = max_over_ranks(total_ms / steps, world)
+    rec = {"config": {**wl.config(), "parallelism": f"sequence parallel over {world} GPU(s): video tokens "
+                                                   f"sharded, NCCL all-gather of the chunk K/V at attention"},
+           "us_per_block": round(ms * 1e3, 1), "steps": steps,
+           "tflops": round(wl.flops() / (ms * 1e-3) / 1e12, 1),
+           "timing": "eager steps (NCCL collective and library attention inside), CUDA events, max over ranks"}
+    if world > 1:
+        rec["allgather"] = time_allgather(wl, st, world, rank)
+        exposed = []
+        for _ in range(3):
+            ev = {}
+            st["events"] = ev
+            wl.step(st)
+            torch.cuda.synchronize()
+            exposed.append(max(0.0, ev["overlap_end"].elapsed_time(ev["gather_end"])))
+        st.pop("events")
+        ex = max_over_ranks(statistics.median(exposed), world)
+        g_us = rec["allgather"]["us"]
+        rec["allgather"].update(exposed_us=round(ex * 1e3, 1),
+                                hidden_frac=round(max(0.0, 1 - ex * 1e3 / g_us), 3) if g_us > 0 else None)
+    del st
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_ours(args, wl: Workload):
+    world, rank, local = dist_init(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     if isinstance(wl, Chain):
-        line.update(metric="µs per DiT-block op chain per chunk", value=round(ms * 1e3, 1), unit="us",
-                    higher_is_better=False, scaling="strong")
-        line["config"]["parallelism"] = (f"sequence parallel over {world} GPUs: video tokens sharded, "
-                                         f"NCCL all-gather of the chunk K/V at the attention boundary")
-        line["config"]["flops_per_step"] = wl.flops()
-        line["achieved_tflops"] = round(wl.flops() / (ms * 1e-3) / 1e12, 1)
-        line["roofline"] = {"bound": "tensor", "achieved": line["achieved_tflops"],
-                            "peak": float(json.loads((REPO / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
-                            if (REPO / "MEASURED_PEAKS.json").exists() else 1590.0,
-                            "unit": "TFLOP/s", "note": "whole block (GEMMs FP8, attention bf16 library) per GPU "
-                                                      "set vs the measured bf16 dense peak of one GPU x N",
-                            "traffic": None}
-        line["roofline"]["peak"] *= world
-        line["roofline"]["frac"] = round(line["achieved_tflops"] / line["roofline"]["peak"], 4)
-        line["e2e"].update(value=round(e2e_step_ms * 1e3, 1), unit="us")
-        line.pop("pct_of_8TBs")
-        if gather is not None:
-            line["allgather"] = gather
-        line["cpu_baseline"] = {"value": None, "unit": "us", "cores": os.cpu_count(), "kind": "port",
-                                "sample": "not run: the block is ~10 TFLOP (attention over 54k keys), hours of "
-                                          "host-CPU time; the per-op CPU baselines are in the per-op lines"}
-        print(json.dumps(line), flush=True)
+        line = {"metric": "µs per DiT-block op chain per chunk", "unit": "us", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (random-init weights)", "config": wl.config()}
+        rec = run_chain(args, world, rank, dev)
+        line.update(value=rec["us_per_block"], ms_per_step=round(rec["us_per_block"] / 1e3, 4), chain=rec)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
         _finish(world)
         return
-    if isinstance(wl, Gemm):
-        line["metric"] = "FP8 GEMM TFLOP/s"
-        line["unit"] = "TFLOP/s"
-        line["value"] = round(world * wl.flops() / (ms * 1e-3) / 1e12, 2)
-        line["roofline"] = line_tensor
-        line["e2e"]["value"] = round(world * wl.flops() / (e2e_step_ms * 1e-3) / 1e12, 3)
-        line["e2e"]["unit"] = "TFLOP/s"
-        line.pop("pct_of_8TBs")
+    line = run_headline(args, wl, world, rank, local, dev)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl)
-        if isinstance(wl, Gemm):
-            cb = line["cpu_baseline"]
-            x = wl.make_cpu(1)
-            t0 = time.perf_counter()
-            wl.cpu_step(x)
-            el = time.perf_counter() - t0
-            cb.update(value=round(2 * x["rows"] * wl.N * wl.K / el / 1e12, 5), unit="TFLOP/s",
-                      sample=f"{x['rows']} rows of A against the full B, fp32 dequantised GEMM, "
-                             f"{torch.get_num_threads()} threads")
-    print(json.dumps(line), flush=True)
+    if not args.no_chain:
+        line["chain"] = run_chain(args, world, rank, dev)
+    if world == 1 and not args.no_per_op and args.workload == "qkv_pack":
+        line["per_op"] = run_per_op(args, dev, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     _finish(world)
 
 
@@ -831,7 +880,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qkv_pack", choices=sorted(workloads()))
-    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the ~10 s CPU baseline leg")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-per-op", action="store_true", help="skip the per-op records")
+    ap.add_argument("--no-chain", action="store_true", help="skip the per-block chain record")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -186,6 +186,29 @@ JO_API int jo_qkv_norm_rope_pack(void* out_q, void* out_k, void* out_v, void* k_
                           int64_t head_dim, const void* q_weight, const void* k_weight,
                           const void* cos, const void* sin, float eps, void* stream);
 
+/* jo_qkv_norm_rope_pack from and to host memory, pipelined: the qkv rows are
+ * uploaded chunk_tokens tokens at a time on h2d_stream, each chunk is packed on
+ * `stream` once its upload has landed, and its q/k/v rows are downloaded on
+ * d2h_stream once packed, so both directions of the host link and the kernel
+ * overlap (one cudaMemcpyAsync per chunk for the input, one per output tensor
+ * per chunk; a 2-D copy for head-major outputs).  host_qkv: bf16 [tokens,
+ * 3*heads*head_dim] contiguous; host_q/k/v and dev_q/k/v share one layout,
+ * head-major [heads, tokens, D] (out_stride_h = tokens*D, out_stride_t = D) or
+ * token-major [tokens, heads, D] (D, heads*D).  dev_qkv/dev_q/k/v: caller-owned
+ * device staging of the same sizes.  Host buffers should be pinned (pageable
+ * memory works but serialises the copies).  The copy streams wait for the work
+ * already queued on `stream`, and `stream` waits for the last download before
+ * anything queued after the call: synchronising `stream` covers the whole call.
+ * h2d_stream and d2h_stream must be non-null (not the legacy default stream).
+ * Replaces, for a host-resident chunk, the upload + jo_qkv_norm_rope_pack +
+ * download that a caller would otherwise issue back to back on one stream. */
+JO_API int jo_qkv_norm_rope_pack_host(void* host_q, void* host_k, void* host_v, int64_t out_stride_h,
+                                      int64_t out_stride_t, const void* host_qkv, void* dev_q, void* dev_k,
+                                      void* dev_v, void* dev_qkv, int64_t tokens, int64_t heads, int64_t head_dim,
+                                      const void* q_weight, const void* k_weight, const void* cos, const void* sin,
+                                      float eps, int64_t chunk_tokens, void* stream, void* h2d_stream,
+                                      void* d2h_stream);
+
 /* gated residual: out = residual + x * gate (fp32 math, one rounding); gate is
  * [gate_rows, cols] with gate_rows in {1, rows}.
  * Replaces fused_add_gate = torch.addcmul
@@ -247,7 +270,10 @@ JO_API int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void*
  * shared by every call on a device: calls whose kernels overlap on the GPU (other
  * streams, other threads) race on it.  The array's address is looked up with
  * cudaGetSymbolAddress on the first call on each device (with that device
- * current); make that first call before any stream capture.  Allocates nothing. */
+ * current), and again on the first call after the device's context was
+ * re-created (cudaDeviceReset); make that first call before any stream capture:
+ * a lookup requested while `stream` is capturing returns JO_ERR_INVALID with a
+ * message saying so.  Allocates nothing. */
 JO_API int jo_timestep_mlp_noalloc(void* vec, const float* t, int64_t batch, const void* w1, const void* b1,
                                    int64_t freq_dim, int64_t dim, const void* w2, const void* b2, const void* w3,
                                    const void* b3, int64_t proj_dim, float max_period, void* stream);

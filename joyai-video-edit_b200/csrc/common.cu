@@ -1,5 +1,7 @@
 // Host-side plumbing shared by every entry point: error strings, per-device
 // facts, launch accounting.
+#include <cuda.h>  // driver types for the context-id entry points (resolved at run time)
+
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -20,6 +22,36 @@ constexpr int kMaxDevices = 64;
 jo::DeviceInfo g_info[kMaxDevices];
 std::once_flag g_info_once[kMaxDevices];
 int g_info_status[kMaxDevices];
+jo::SymbolCache g_fault_cache;
+
+// Unique id of the calling thread's current context (0 when unknown), through the
+// driver entry points cuCtxGetCurrent / cuCtxGetId resolved once via the runtime.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
+std::once_flag g_drv_once;
+uint64_t context_id() {
+  std::call_once(g_drv_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", (void**)&g_ctx_current, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      g_ctx_current = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", (void**)&g_ctx_id, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      g_ctx_id = nullptr;
+    cudaGetLastError();
+  });
+  if (!g_ctx_current || !g_ctx_id) return 0;
+  CUcontext c = nullptr;
+  if (g_ctx_current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_id(c, &id) != CUDA_SUCCESS) return 0;
+  return (uint64_t)id + 1;  // never 0
+}
+std::mutex g_symbol_mu;
 }  // namespace
 
 namespace jo {
@@ -57,15 +89,49 @@ int device_info(const DeviceInfo** out) {
     if (r == cudaSuccess) r = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
     if (r == cudaSuccess)
       r = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (r == cudaSuccess && d.major == 10) r = cudaGetSymbolAddress((void**)&d.fault, g_jo_faults);
     g_info_status[dev] = (r == cudaSuccess) ? JO_OK : JO_ERR_CUDA;
   });
   if (g_info_status[dev] != JO_OK) return fail(JO_ERR_CUDA, "device %d: attribute query failed", dev);
-  const DeviceInfo& d = g_info[dev];
+  DeviceInfo& d = g_info[dev];
   if (d.major != 10 || d.minor != 0)
     return fail(JO_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a only", dev,
                 d.major, d.minor);
+  // the fault counter's address in the device's current context (looked up again
+  // if the context was re-created)
+  void* fault = nullptr;
+  if (int s = symbol_address(g_fault_cache, &g_jo_faults, dev, nullptr, &fault, "fault counter")) return s;
+  d.fault = static_cast<unsigned int*>(fault);
   *out = &d;
+  return JO_OK;
+}
+
+int symbol_address(SymbolCache& cache, const void* symbol, int dev, cudaStream_t stream, void** out,
+                   const char* what) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(JO_ERR_CUDA, "%s: device index %d out of range", what, dev);
+  const uint64_t ctx = context_id();
+  if (ctx != 0 && cache.ctx[dev].load(std::memory_order_acquire) == ctx) {
+    *out = cache.addr[dev].load(std::memory_order_relaxed);
+    return JO_OK;
+  }
+  if (stream != nullptr) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) cudaGetLastError();
+    if (cs != cudaStreamCaptureStatusNone)
+      return fail(JO_ERR_INVALID,
+                  "%s: the first call on device %d (in its current context) must come before any stream "
+                  "capture: it looks up the device address of a static array",
+                  what, dev);
+  }
+  std::lock_guard<std::mutex> lock(g_symbol_mu);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, symbol);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(JO_ERR_CUDA, "%s: cudaGetSymbolAddress failed on device %d: %s", what, dev, cudaGetErrorString(e));
+  }
+  cache.addr[dev].store(p, std::memory_order_relaxed);
+  cache.ctx[dev].store(context_id(), std::memory_order_release);  // 0 (unknown) keeps looking up every call
+  *out = p;
   return JO_OK;
 }
 

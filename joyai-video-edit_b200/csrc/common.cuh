@@ -30,6 +30,18 @@ struct DeviceInfo {
   unsigned int* fault;  // device address of this device's fault counter
 };
 int device_info(const DeviceInfo** out);
+// Device address of a __device__ symbol (its host-side shadow `symbol`) on the
+// current device `dev`, cached per device.  The cache is keyed by the device's
+// context: a context created anew (after cudaDeviceReset, the module is loaded
+// again and the symbol may move) is looked up again.  `stream` (may be null) is
+// checked before a lookup: a lookup is refused while it is capturing, since the
+// first lookup on a device may load the module.
+struct SymbolCache {
+  std::atomic<uint64_t> ctx[64];
+  std::atomic<void*> addr[64];
+};
+int symbol_address(SymbolCache& cache, const void* symbol, int dev, cudaStream_t stream, void** out,
+                   const char* what);
 // Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device,
 // once per device: the attribute is per device, so `done` (one per kernel, at
 // the call site) records the devices already set (bit = device ordinal).

@@ -424,9 +424,10 @@ __global__ void __launch_bounds__(kQkWarps * 32, 1)
       }
     }
   }
-  // error path only (a wait expired): copies issued for later units must land
+  // error path only (a wait expired at unit kk): every copy issued, unit kk's
+  // included, must have landed (or its wait expired too) before the CTA exits
   if (lane == 0 && warp + kk * kQkWarps < units)
-    for (int jj = kk + 1; jj < kk + kQkSlots && warp + jj * kQkWarps < units; ++jj)
+    for (int jj = kk; jj < kk + kQkSlots && warp + jj * kQkWarps < units; ++jj)
       mbar_wait(bar0 + 8u * (uint32_t)(jj % kQkSlots), (uint32_t)((jj / kQkSlots) & 1), fault);
 }
 

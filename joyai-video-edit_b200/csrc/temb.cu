@@ -165,9 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       issue(k + m);
     }
   }
-  // error path only (a wait expired at unit k): copies issued for later units must land
+  // error path only (a wait expired at unit k): every copy issued, unit k's
+  // included, must have landed (or its wait expired too) before the CTA exits
   if (lane == 0 && warp + k * kWarps < units)
-    for (int j = k + 1; j < k + m && warp + j * kWarps < units; ++j)
+    for (int j = k; j < k + m && warp + j * kWarps < units; ++j)
       mbar_wait(bar0 + 8u * (uint32_t)(j % m), (uint32_t)((j / m) & 1), fault);
 }
 
@@ -307,24 +308,12 @@ int jo_timestep_mlp_noalloc(void* vec, const float* t, int64_t batch, const void
   if (2 * batch * dim > kStaticScratchElems)
     return fail(JO_ERR_SHAPE, "timestep_mlp_noalloc: batch * dim = %lld exceeds the static scratch limit of %lld",
                 (long long)(batch * dim), (long long)(kStaticScratchElems / 2));
-  // the array's address on the current device, looked up once per device
-  static std::mutex mu;
-  static void* addr[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-    return fail(JO_ERR_CUDA, "timestep_mlp_noalloc: no current device");
-  void* ptr;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-      const cudaError_t e = cudaGetSymbolAddress(&addr[dev], g_temb_scratch);
-      if (e != cudaSuccess) {
-        addr[dev] = nullptr;
-        return fail(JO_ERR_CUDA, "timestep_mlp_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-      }
-    }
-    ptr = addr[dev];
-  }
+  // the array's address on the current device: looked up on the first call on each
+  // device (and again if the device's context is re-created), cached otherwise
+  static SymbolCache cache;
+  void* ptr = nullptr;
+  if (int s = symbol_address(cache, g_temb_scratch, di->ordinal, (cudaStream_t)stream, &ptr, "timestep_mlp_noalloc"))
+    return s;
   return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
                           reinterpret_cast<__nv_bfloat16*>(ptr), max_period, (cudaStream_t)stream, di);
 }

@@ -8,6 +8,7 @@
 // A non-zero status becomes a RuntimeError carrying jo_last_error().
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
 #include <torch/all.h>
 #include <torch/library.h>
 
@@ -55,12 +56,24 @@ jo_view4 view4(const torch::Tensor& t) {
 }
 jo_view4 no_view() { return jo_view4{nullptr, 0, 0, 0}; }
 
+// Every tensor operand must be a CUDA tensor on the op's device (the device of
+// `anchor`): a host pointer or another device's pointer handed to a kernel would
+// fault the GPU instead of raising here.
+void check_dev(const torch::Tensor& t, const torch::Tensor& anchor, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.device() == anchor.device(), name, " is on ", t.device(), " but the op runs on ", anchor.device());
+}
+void check_dev(const c10::optional<torch::Tensor>& t, const torch::Tensor& anchor, const char* name) {
+  if (t.has_value() && t->defined()) check_dev(*t, anchor, name);
+}
+
 // ------------------------------------------------------------------ drop-in ops
 
 // joyomni_ops/csrc/rmsnorm.cu:107-126
 torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& weight, double eps) {
   JO_CHECK_CUDA(x);
   JO_CHECK_CUDA(weight);
+  check_dev(weight, x, "weight");
   TORCH_CHECK(x.dim() == 2, "x must be 2D [M, N]");
   TORCH_CHECK(x.stride(-1) == 1, "x last dim must be contiguous");
   TORCH_CHECK(weight.dim() == 1 && weight.numel() == x.size(1), "weight must be 1D [N]");
@@ -76,6 +89,8 @@ torch::Tensor rmsnorm(const torch::Tensor& x, const torch::Tensor& weight, doubl
 
 void check_mod(const torch::Tensor& x, const torch::Tensor& scale, const torch::Tensor& shift) {
   const int64_t M = x.size(0), N = x.size(1);
+  check_dev(scale, x, "scale");
+  check_dev(shift, x, "shift");
   TORCH_CHECK(scale.dim() == 2 && shift.dim() == 2, "scale/shift must be 2D [M, N] or [1, N]");
   TORCH_CHECK(scale.size(0) == shift.size(0), "scale/shift row counts must match");
   TORCH_CHECK(scale.size(0) == 1 || scale.size(0) == M,
@@ -90,6 +105,8 @@ void check_mod(const torch::Tensor& x, const torch::Tensor& scale, const torch::
 void check_affine(const torch::Tensor& x, const c10::optional<torch::Tensor>& gamma,
                   const c10::optional<torch::Tensor>& beta) {
   const int64_t N = x.size(1);
+  check_dev(gamma, x, "gamma");
+  check_dev(beta, x, "beta");
   if (gamma.has_value() && gamma->defined()) {
     TORCH_CHECK(gamma->numel() == N, "gamma must be length N");
     TORCH_CHECK(gamma->is_contiguous() && gamma->dtype() == x.dtype(), "gamma must be contiguous with x's dtype");
@@ -140,6 +157,12 @@ void fused_qk_norm_rope_3d_paired(torch::Tensor& q, torch::Tensor& k, int64_t se
   JO_CHECK_INPUT(k_weight, torch::kBFloat16);
   JO_CHECK_INPUT(cos, torch::kBFloat16);
   JO_CHECK_INPUT(sin, torch::kBFloat16);
+  check_dev(k, q, "k");
+  check_dev(q_weight, q, "q_weight");
+  check_dev(k_weight, q, "k_weight");
+  check_dev(cos, q, "cos");
+  check_dev(sin, q, "sin");
+  check_dev(k_pre_rope_opt, q, "k_pre_rope");
   const int64_t batch = q.size(0), head_dim = q.size(2);
   TORCH_CHECK(q.size(1) == seq_len * num_heads, "q.size(1) must equal seq_len*num_heads");
   TORCH_CHECK(q_weight.size(0) == head_dim && k_weight.size(0) == head_dim, "weight size must match head_dim");
@@ -195,6 +218,15 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> fused_joint_qkv_pack(
               "text Q/K/V lengths must match and be positive");
   JO_CHECK_INPUT(txt_q_weight, torch::kBFloat16);
   JO_CHECK_INPUT(txt_k_weight, torch::kBFloat16);
+  check_dev(img_k, img_q, "img_k");
+  check_dev(img_v, img_q, "img_v");
+  check_dev(txt_q, img_q, "txt_q");
+  check_dev(txt_k, img_q, "txt_k");
+  check_dev(txt_v, img_q, "txt_v");
+  check_dev(cached_k_opt, img_q, "cached_k");
+  check_dev(cached_v_opt, img_q, "cached_v");
+  check_dev(txt_q_weight, img_q, "txt_q_weight");
+  check_dev(txt_k_weight, img_q, "txt_k_weight");
   TORCH_CHECK(txt_q_weight.dim() == 1 && txt_q_weight.numel() == head_dim, "txt_q_weight must be [head_dim]");
   TORCH_CHECK(txt_k_weight.dim() == 1 && txt_k_weight.numel() == head_dim, "txt_k_weight must be [head_dim]");
   TORCH_CHECK(cached_k_opt.has_value() == cached_v_opt.has_value(),
@@ -252,6 +284,11 @@ std::tuple<torch::Tensor, torch::Tensor> fused_cached_kv_pack(const torch::Tenso
   }
   JO_CHECK_INPUT(cos, torch::kFloat32);
   JO_CHECK_INPUT(sin, torch::kFloat32);
+  check_dev(value0, key0, "value0");
+  check_dev(key1_opt, key0, "key1");
+  check_dev(value1_opt, key0, "value1");
+  check_dev(cos, key0, "cos");
+  check_dev(sin, key0, "sin");
   TORCH_CHECK(cos.sizes() == sin.sizes(), "cos/sin shapes must match");
   TORCH_CHECK(cos.numel() == (len0 + len1) * head_dim, "cos/sin must contain [total_cache_len, head_dim], got ",
               cos.sizes());
@@ -270,6 +307,8 @@ void sgl_per_token_quant_fp8(torch::Tensor input, torch::Tensor output_q, torch:
   JO_CHECK_CONTIGUOUS(input);
   JO_CHECK_CUDA(output_q);
   JO_CHECK_CUDA(output_s);
+  check_dev(output_q, input, "output_q");
+  check_dev(output_s, input, "output_s");
   TORCH_CHECK(input.dim() == 2, "input must be 2D [num_tokens, hidden_dim]");
   const int64_t num_tokens = input.size(0), hidden_dim = input.size(1);
   TORCH_CHECK(hidden_dim % 4 == 0, "hidden_dim must be divisible by 4, got ", hidden_dim);
@@ -312,6 +351,10 @@ torch::Tensor fp8_scaled_mm(const torch::Tensor& mat_a, const torch::Tensor& mat
   TORCH_CHECK(scales_b.is_contiguous(), "scales_b msut be contiguous");
   TORCH_CHECK(scales_a.scalar_type() == torch::kFloat32, "scales_a must be Float32");
   TORCH_CHECK(scales_b.scalar_type() == torch::kFloat32, "scales_b must be Float32");
+  check_dev(mat_b, mat_a, "mat_b");
+  check_dev(scales_a, mat_a, "scales_a");
+  check_dev(scales_b, mat_a, "scales_b");
+  check_dev(bias, mat_a, "bias");
   if (bias) {
     TORCH_CHECK(bias->numel() == mat_b.size(1), "size of bias is not matched");
     TORCH_CHECK(bias->is_contiguous(), "bias must be contiguous");
@@ -348,6 +391,12 @@ torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const tor
   TORCH_CHECK(scales_b.numel() == mat_b.size(1) && scales_b.is_contiguous() &&
                   scales_b.scalar_type() == torch::kFloat32,
               "scales_b must be contiguous Float32 with one value per column of mat_b");
+  check_dev(mat_b, mat_a, "mat_b");
+  check_dev(scales_a, mat_a, "scales_a");
+  check_dev(scales_b, mat_a, "scales_b");
+  check_dev(bias, mat_a, "bias");
+  check_dev(residual, mat_a, "residual");
+  check_dev(gate, mat_a, "gate");
   if (bias) {
     TORCH_CHECK(bias->numel() == mat_b.size(1) && bias->is_contiguous() && bias->dtype() == out_dtype,
                 "bias must be contiguous [N] of the output dtype");
@@ -399,6 +448,10 @@ std::pair<int64_t, int64_t> check_qkv_pack(const torch::Tensor& qkv, int64_t num
   TORCH_CHECK(D == 64 || D == 128 || D == 256, "head_dim must be 64, 128 or 256, got ", D);
   JO_CHECK_INPUT(q_weight, torch::kBFloat16);
   JO_CHECK_INPUT(k_weight, torch::kBFloat16);
+  check_dev(q_weight, qkv, "q_weight");
+  check_dev(k_weight, qkv, "k_weight");
+  check_dev(cos, qkv, "cos");
+  check_dev(sin, qkv, "sin");
   TORCH_CHECK(q_weight.numel() == D && k_weight.numel() == D, "weight size must match head_dim");
   const bool hc = cos.has_value() && cos->defined(), hs = sin.has_value() && sin->defined();
   TORCH_CHECK(hc == hs, "cos and sin must both be given (RoPE) or both be None (text rows, no rotation)");
@@ -425,6 +478,7 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> qkv_norm_rope_pack(
   void* pre = nullptr;
   if (k_pre_rope.has_value() && k_pre_rope->defined()) {
     JO_CHECK_INPUT(*k_pre_rope, torch::kBFloat16);
+    check_dev(*k_pre_rope, qkv, "k_pre_rope");
     TORCH_CHECK(k_pre_rope->sizes() == k.sizes(), "k_pre_rope must have the output shape ", k.sizes());
     pre = k_pre_rope->data_ptr();
   }
@@ -446,6 +500,7 @@ void qkv_norm_rope_pack_into(const torch::Tensor& qkv, int64_t num_heads, const 
   const auto [L, D] = check_qkv_pack(qkv, num_heads, q_weight, k_weight, cos, sin);
   for (const torch::Tensor* t : {&q_out, &k_out, &v_out}) {
     JO_CHECK_CUDA(*t);
+    check_dev(*t, qkv, "q/k/v output");
     JO_CHECK_DTYPE(*t, torch::kBFloat16);
     TORCH_CHECK(t->dim() == 3 && t->size(0) == L && t->size(1) == num_heads && t->size(2) == D,
                 "outputs must be [tokens, heads, head_dim] views, got ", t->sizes());
@@ -457,6 +512,57 @@ void qkv_norm_rope_pack_into(const torch::Tensor& qkv, int64_t num_heads, const 
                                  q_out.stride(0), qkv.data_ptr(), qkv.stride(0), L, num_heads, D, q_weight.data_ptr(),
                                  k_weight.data_ptr(), opt_ptr(cos), opt_ptr(sin), (float)eps, stream_of(qkv)),
            "qkv_norm_rope_pack_into");
+}
+
+// qkv_norm_rope_pack from pinned host memory to pinned host memory: the upload of
+// each token chunk, its pack and the download of its q/k/v overlap on three
+// streams (the current stream and two from the pool).  Device staging buffers
+// come from the caching allocator on the current stream; the call returns with
+// every copy ordered before later work on the current stream.
+void qkv_norm_rope_pack_host(const torch::Tensor& qkv_host, int64_t num_heads, const torch::Tensor& q_weight,
+                             const torch::Tensor& k_weight, const c10::optional<torch::Tensor>& cos,
+                             const c10::optional<torch::Tensor>& sin, double eps, bool head_major,
+                             torch::Tensor& q_host, torch::Tensor& k_host, torch::Tensor& v_host,
+                             int64_t chunk_tokens) {
+  TORCH_CHECK(!qkv_host.is_cuda() && qkv_host.is_pinned(), "qkv_host must be a pinned host tensor");
+  TORCH_CHECK(qkv_host.dim() == 2 && qkv_host.is_contiguous(), "qkv_host must be contiguous [tokens, 3*heads*head_dim]");
+  JO_CHECK_DTYPE(qkv_host, torch::kBFloat16);
+  TORCH_CHECK(num_heads > 0 && qkv_host.size(1) % (3 * num_heads) == 0, "qkv width must be 3*num_heads*head_dim");
+  const int64_t L = qkv_host.size(0), D = qkv_host.size(1) / (3 * num_heads);
+  JO_CHECK_INPUT(q_weight, torch::kBFloat16);
+  JO_CHECK_INPUT(k_weight, torch::kBFloat16);
+  check_dev(k_weight, q_weight, "k_weight");
+  check_dev(cos, q_weight, "cos");
+  check_dev(sin, q_weight, "sin");
+  const bool hc = cos.has_value() && cos->defined(), hs = sin.has_value() && sin->defined();
+  TORCH_CHECK(hc == hs, "cos and sin must both be given (RoPE) or both be None (text rows, no rotation)");
+  if (hc) {
+    JO_CHECK_INPUT(*cos, torch::kBFloat16);
+    JO_CHECK_INPUT(*sin, torch::kBFloat16);
+    TORCH_CHECK(cos->dim() == 2 && cos->size(0) == L && cos->size(1) == D / 2 && sin->sizes() == cos->sizes(),
+                "cos/sin shape must be [tokens, head_dim/2]");
+  }
+  auto shape = head_major ? std::vector<int64_t>{num_heads, L, D} : std::vector<int64_t>{L, num_heads, D};
+  for (const torch::Tensor* t : {&q_host, &k_host, &v_host}) {
+    TORCH_CHECK(!t->is_cuda() && t->is_pinned() && t->is_contiguous(), "q/k/v_host must be contiguous pinned host tensors");
+    JO_CHECK_DTYPE(*t, torch::kBFloat16);
+    TORCH_CHECK(t->sizes() == shape, "q/k/v_host must be ", shape, ", got ", t->sizes());
+  }
+  TORCH_CHECK(chunk_tokens > 0, "chunk_tokens must be positive");
+  const c10::cuda::CUDAGuard guard(q_weight.device());
+  auto dev_qkv = torch::empty({L, qkv_host.size(1)}, q_weight.options());
+  auto dq = torch::empty(shape, q_weight.options());
+  auto dk = torch::empty(shape, q_weight.options());
+  auto dv = torch::empty(shape, q_weight.options());
+  auto in = c10::cuda::getStreamFromPool(false, q_weight.get_device());
+  auto out = c10::cuda::getStreamFromPool(false, q_weight.get_device());
+  const int64_t sh = head_major ? L * D : D, st = head_major ? D : num_heads * D;
+  jo_check(jo_qkv_norm_rope_pack_host(q_host.data_ptr(), k_host.data_ptr(), v_host.data_ptr(), sh, st,
+                                      qkv_host.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                      dev_qkv.data_ptr(), L, num_heads, D, q_weight.data_ptr(), k_weight.data_ptr(),
+                                      opt_ptr(cos), opt_ptr(sin), (float)eps, chunk_tokens, stream_of(q_weight),
+                                      (void*)in.stream(), (void*)out.stream()),
+           "qkv_norm_rope_pack_host");
 }
 
 std::tuple<torch::Tensor, torch::Tensor> gelu_quant_fp8(const torch::Tensor& x) {
@@ -477,6 +583,8 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> gated_residual_norm_scal
     const torch::Tensor& shift, int64_t norm_type, double eps) {
   JO_CHECK_CUDA(residual);
   JO_CHECK_CUDA(x);
+  check_dev(residual, x, "residual");
+  check_dev(gate, x, "gate");
   TORCH_CHECK(residual.sizes() == x.sizes(), "residual and x must have the same shape");
   TORCH_CHECK(residual.dtype() == x.dtype() && x.dtype() == gate.dtype(), "dtypes must match");
   TORCH_CHECK(norm_type == 0 || norm_type == 1, "norm_type must be 0 (layer) or 1 (rms)");
@@ -505,6 +613,8 @@ torch::Tensor gated_residual(const torch::Tensor& residual, const torch::Tensor&
   JO_CHECK_CUDA(residual);
   JO_CHECK_CUDA(x);
   JO_CHECK_CUDA(gate);
+  check_dev(residual, x, "residual");
+  check_dev(gate, x, "gate");
   TORCH_CHECK(residual.sizes() == x.sizes(), "residual and x must have the same shape");
   TORCH_CHECK(residual.dtype() == x.dtype() && x.dtype() == gate.dtype(), "dtypes must match");
   const int64_t N = x.size(-1);
@@ -525,6 +635,8 @@ std::tuple<torch::Tensor, torch::Tensor> gated_residual_norm_scale_shift(
     const torch::Tensor& shift, int64_t norm_type, double eps) {
   JO_CHECK_CUDA(residual);
   JO_CHECK_CUDA(x);
+  check_dev(residual, x, "residual");
+  check_dev(gate, x, "gate");
   TORCH_CHECK(residual.sizes() == x.sizes(), "residual and x must have the same shape");
   TORCH_CHECK(residual.dtype() == x.dtype() && x.dtype() == gate.dtype(), "dtypes must match");
   TORCH_CHECK(norm_type == 0 || norm_type == 1, "norm_type must be 0 (layer) or 1 (rms)");
@@ -560,6 +672,7 @@ torch::Tensor gelu_tanh(const torch::Tensor& x) {
 torch::Tensor silu_mul(const torch::Tensor& a, const torch::Tensor& b) {
   JO_CHECK_CUDA(a);
   JO_CHECK_CUDA(b);
+  check_dev(b, a, "b");
   TORCH_CHECK(a.sizes() == b.sizes() && a.dtype() == b.dtype(), "a and b must match in shape and dtype");
   const int64_t N = a.size(-1);
   auto a2 = as_rows(a, N, "a");
@@ -628,6 +741,7 @@ std::tuple<torch::Tensor, torch::Tensor> rmsnorm_quant_fp8(const torch::Tensor& 
                                                            double eps) {
   JO_CHECK_CUDA(x);
   TORCH_CHECK(x.dim() == 2 && x.stride(-1) == 1, "x must be 2D [M, N] with contiguous rows");
+  check_dev(weight, x, "weight");
   TORCH_CHECK(weight.dim() == 1 && weight.numel() == x.size(1) && weight.dtype() == x.dtype() &&
                   weight.is_contiguous(),
               "weight must be contiguous [N] of x's dtype");
@@ -692,6 +806,10 @@ TORCH_LIBRARY(joyomni_ops, m) {
   m.def(
       "qkv_norm_rope_pack_into(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
       "Tensor? sin, float eps, Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out) -> ()");
+  m.def(
+      "qkv_norm_rope_pack_host(Tensor qkv_host, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
+      "Tensor? sin, float eps, bool head_major, Tensor(a!) q_host, Tensor(b!) k_host, Tensor(c!) v_host, "
+      "int chunk_tokens) -> ()");
   m.def("gelu_quant_fp8(Tensor x) -> (Tensor, Tensor)");
   m.def(
       "gated_residual_norm_scale_shift_quant_fp8(Tensor residual, Tensor x, Tensor gate, Tensor? gamma, "
@@ -725,6 +843,7 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("fp8_scaled_mm_gated_residual", &fp8_scaled_mm_gated_residual);
   m.impl("qkv_norm_rope_pack", &qkv_norm_rope_pack);
   m.impl("qkv_norm_rope_pack_into", &qkv_norm_rope_pack_into);
+  m.impl("qkv_norm_rope_pack_host", &qkv_norm_rope_pack_host);
   m.impl("gelu_quant_fp8", &gelu_quant_fp8);
   m.impl("gated_residual_norm_scale_shift_quant_fp8", &gated_residual_norm_scale_shift_quant_fp8);
   m.impl("gated_residual", &gated_residual);

@@ -49,6 +49,7 @@ __all__ = [
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
     "qkv_norm_rope_pack_into",
+    "qkv_norm_rope_pack_host",
     "gelu_quant_fp8",
     "gated_residual_norm_scale_shift_quant_fp8",
     "library_path",
@@ -120,6 +121,12 @@ def _fake_qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, 
 
 @torch.library.register_fake("joyomni_ops::qkv_norm_rope_pack_into")
 def _fake_qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out):
+    return None
+
+
+@torch.library.register_fake("joyomni_ops::qkv_norm_rope_pack_host")
+def _fake_qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, eps, head_major, q_host, k_host,
+                                  v_host, chunk_tokens):
     return None
 
 
@@ -248,6 +255,15 @@ def qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps=1e-6, h
 def qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, q_out, k_out, v_out, eps=1e-6):
     """qkv_norm_rope_pack writing into [L, H, D] views (e.g. slices of persistent Q / KV buffers)."""
     _ops.qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out)
+
+
+def qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, q_host, k_host, v_host, eps=1e-6,
+                            head_major=True, chunk_tokens=1350):
+    """qkv_norm_rope_pack from a pinned host qkv [L, 3*H*D] into pinned host q/k/v
+    ([H, L, D] head-major, else [L, H, D]); weights and cos/sin on the GPU.  Uploads,
+    packs and downloads overlap chunk by chunk (chunk_tokens tokens each)."""
+    _ops.qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, eps, head_major, q_host, k_host,
+                                 v_host, chunk_tokens)
 
 
 def gelu_quant_fp8(x):

@@ -183,6 +183,12 @@ def _stream_out(x, attn, w: StreamWeights, m, trace=None, tag=""):
     return out
 
 
+def _event(stream) -> torch.cuda.Event:
+    e = torch.cuda.Event(enable_timing=True)
+    e.record(stream)
+    return e
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """Non-causal joint attention on token-major [S, H, D] buffers -> [Sq, H*D]."""
     out = F.scaled_dot_product_attention(q.unsqueeze(0).transpose(1, 2), k.unsqueeze(0).transpose(1, 2),
@@ -192,7 +198,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor
 
 def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                   w: BlockWeights, bufs: KVBuffers, group=None, rank: int = 0,
-                  side_stream: Optional[torch.cuda.Stream] = None, trace: Optional[dict] = None):
+                  side_stream: Optional[torch.cuda.Stream] = None, trace: Optional[dict] = None,
+                  events: Optional[dict] = None):
     """One double-stream block for one chunk.
 
     img: bf16 [L_local, D] (this rank's video tokens), txt: bf16 [L_txt, D],
@@ -200,6 +207,10 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
     for this rank's video tokens.  The cache rows of ``bufs.k/v`` hold the prior chunks.
     Returns (img_out [L_local, D], txt_out [L_txt, D]).  ``trace`` (a dict), if
     given, receives every intermediate tensor (for stage-by-stage parity tests).
+    ``events`` (a dict), if given with a group, receives timing CUDA events:
+    "gather_start" / "gather_end" around the K/V all-gather on the side stream and
+    "overlap_end" on the compute stream once the work that overlaps it is queued,
+    so the gather's exposed time is max(0, overlap_end -> gather_end).
     """
     H = w.heads
     L = img.shape[0]
@@ -213,11 +224,17 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
         side = side_stream or torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
+            if events is not None:
+                events["gather_start"] = _event(side)
             gather_chunk_kv(bufs, rank, group)
+            if events is not None:
+                events["gather_end"] = _event(side)
         gathered = side
     _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows()], bufs.v[bufs.txt_kv_rows()],
                 trace, "txt")
     if gathered is not None:
+        if events is not None:
+            events["overlap_end"] = _event(torch.cuda.current_stream())
         torch.cuda.current_stream().wait_stream(gathered)
     attn = attention(bufs.q, bufs.k, bufs.v)
     if trace is not None:

@@ -207,6 +207,45 @@ def qk_norm_rope_shim(q, k, qw, kw, cos, sin, eps):
     return apply(qn), apply(kn), kn
 
 
+def rope_video_tables(frames: int, height: int, width: int, t0: int, dims=(44, 42, 42), theta: float = 10000.0):
+    """(cos_full, sin_full) fp32 [F*H*W, sum(dims)] and (cos_half, sin_half) bf16 [F*H*W, sum(dims)/2]
+    for a frame-major (t, h, w) token grid whose frames start at t0.
+
+    Per axis get_1d_rotary_pos_embed (deploy/xvideo/models/dit/rope.py:31-52: freqs =
+    1/theta^(arange(0, d, 2)/d), outer product with the positions, cos/sin repeat-interleaved),
+    concatenated over (t, h, w) as get_rotary_pos_embed_from_ids does (dit.py:896-934), then
+    prepare_fused_rope's every-other-column bf16 tables (sgl_fused_ops.py:94-119).
+    """
+    t = (torch.arange(frames, dtype=torch.float32) + float(t0)).repeat_interleave(height * width)
+    h = torch.arange(height, dtype=torch.float32).repeat_interleave(width).repeat(frames)
+    w = torch.arange(width, dtype=torch.float32).repeat(frames * height)
+    cos_l, sin_l = [], []
+    for d, pos in zip(dims, (t, h, w)):
+        freqs = 1.0 / (theta ** (torch.arange(0, d, 2)[: d // 2].float() / d))
+        ang = torch.outer(pos, freqs)
+        cos_l.append(ang.cos().repeat_interleave(2, dim=1))
+        sin_l.append(ang.sin().repeat_interleave(2, dim=1))
+    cos, sin = torch.cat(cos_l, 1), torch.cat(sin_l, 1)
+    return (cos, sin), (cos[:, ::2].to(torch.bfloat16).contiguous(), sin[:, ::2].to(torch.bfloat16).contiguous())
+
+
+def qkv_pack_reference_path(qkv, num_heads, qw, kw, cos, sin, eps):
+    """Config 1 as the reference computes it without its native ops, step for step.
+
+    The rearrange "B L (K H D) -> K B L H D" of the QKV projection (dit.py:409-411, strided
+    views), the fused_qk_norm_rope_3d fallback (sgl_fused_ops.py:170-199: _torch_rmsnorm of
+    the strided q and k -> bf16, then the full-width rotation in fp32 -> bf16; restated by
+    qk_norm_rope_shim, which the golden vectors pin bit-exactly), and q/k/v materialised
+    head-major [H, L, D] as config 1 asks.  The timed CPU arm of the benchmark.
+    """
+    L = qkv.shape[0]
+    D = qkv.shape[1] // (3 * num_heads)
+    x = qkv.view(1, L, 3, num_heads, D)
+    q, k, v = x.unbind(2)
+    qo, ko, _ = qk_norm_rope_shim(q, k, qw, kw, cos, sin, eps)
+    return tuple(t[0].transpose(0, 1).contiguous() for t in (qo, ko, v))
+
+
 def qkv_norm_rope_pack(qkv, num_heads, qw, kw, cos, sin, eps, head_major=True, with_pre=False):
     """q, k, v (and k_pre_rope) from the QKV projection output in one pass.
 

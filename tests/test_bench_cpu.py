@@ -23,3 +23,27 @@ def test_reference_arm_prints_the_contract_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert "workload" in d["config"]
+
+
+def test_reference_arm_never_loads_this_package():
+    """The reference arm must not map this repository's libraries: it runs the reference's
+    CPU sequence through the oracle alone."""
+    code = ("import sys; sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3']; "
+            "import bench; bench.main(); "
+            "bad = [m for m in sys.modules if m.split('.')[0] == 'joyomni_ops']; "
+            "maps = open('/proc/self/maps').read(); "
+            "assert not bad, bad; assert 'libjoyomni_b200' not in maps and '_C.so' not in maps")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=str(REPO))
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_both_arms_name_the_same_config():
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    for name, wl in bench.workloads().items():
+        assert wl.config()["workload"] == wl.desc
+    d = json.loads([ln for ln in subprocess.run(
+        [sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3"],
+        capture_output=True, text=True, timeout=600, cwd=str(REPO)).stdout.splitlines() if ln.startswith("{")][0])
+    assert d["config"] == bench.workloads()["qkv_pack"].config()

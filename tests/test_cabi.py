@@ -58,12 +58,22 @@ def test_ctypes_binding_covers_header(cabi):
     assert header_symbols() == set(cabi.SIGNATURES), "cabi.SIGNATURES out of sync with include/*.h"
 
 
-def test_integration_table_covers_header():
-    # the maintainer-facing table of entry points names every declared symbol
-    text = (REPO / "INTEGRATION.md").read_text()
-    section = text.split("## 4. Entry points of the C ABI", 1)[1].split("\n## ", 1)[0]
-    listed = set(re.findall(r"`(jo_\w+)`", section))
-    assert header_symbols() == listed, f"INTEGRATION.md table out of sync: {header_symbols() ^ listed}"
+def header_arity():
+    """Parameter count of every entry point, read from the declarations in include/*.h."""
+    arity = {}
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^JO_API\s+[\w\s\*]+?\b(jo_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.M | re.S):
+            params = m.group(2).strip()
+            arity[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return arity
+
+
+def test_ctypes_binding_arity_matches_header(cabi):
+    arity = header_arity()
+    assert set(arity) == header_symbols()
+    wrong = {n: (len(cabi.SIGNATURES[n]), a) for n, a in arity.items() if len(cabi.SIGNATURES[n]) != a}
+    assert not wrong, f"ctypes argument count differs from the header (binding, header): {wrong}"
 
 
 def test_abi_info(cabi):

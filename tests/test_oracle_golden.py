@@ -75,6 +75,24 @@ def test_rope_tables_bit_exact(golden):
         assert torch.equal(cos, c["cos_full"]) and torch.equal(sin, c["sin_full"]), name
         ch, sh = rope.paired_tables(cos, sin)
         assert torch.equal(ch, c["cos_half"]) and torch.equal(sh, c["sin_half"]), name
+        # the oracle's own restatement (the benchmark's CPU arm builds its tables with it)
+        (cf, sf), (ch2, sh2) = ops.rope_video_tables(c["frames"], c["height"], c["width"], c["t0"], c["dims"],
+                                                     c["theta"])
+        assert torch.equal(cf, c["cos_full"]) and torch.equal(sf, c["sin_full"]), name
+        assert torch.equal(ch2, c["cos_half"]) and torch.equal(sh2, c["sin_half"]), name
+
+
+def test_qkv_pack_reference_path(golden):
+    """The benchmark's CPU arm for config 1 equals the reference's fallback on the golden case."""
+    c = golden["qk_norm_rope_shim"]
+    q, k = c["q"], c["k"]
+    B, L, H, D = q.shape
+    v = torch.randn(B, L, H, D, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    qkv = torch.stack((q, k, v), dim=2).reshape(L, 3 * H * D)
+    oq, ok, ov = ops.qkv_pack_reference_path(qkv, H, c["qw"], c["kw"], c["cos"], c["sin"], c["eps"])
+    assert torch.equal(oq, c["q_out"][0].transpose(0, 1))
+    assert torch.equal(ok, c["k_out"][0].transpose(0, 1))
+    assert torch.equal(ov, v[0].transpose(0, 1))
 
 
 def test_qk_norm_rope(golden):

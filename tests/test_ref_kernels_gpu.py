@@ -1,0 +1,149 @@
+"""GPU cross-check against the reference's own CUDA kernels.
+
+oracle/build_ref.py compiles the reference's light kernels (rmsnorm,
+fused_norm_scale_shift, fused_qknorm_rope_3d_kernel, fused_joint_qkv_pack,
+per_token_quant_fp8; joyomni_ops/csrc/*.cu) unmodified into
+oracle/_ref/libjoyomni_ref.so, registered as torch.ops.joyomni_ref.*.  Here both
+implementations run on the same inputs on the same GPU, at the BASELINE shapes and
+at the reference tests' own shapes (joyomni_ops/tests/test_parity_light.py):
+
+* copied rows (V, cache and image rows of the packs): bit-equal;
+* normalised / rotated bf16 outputs: <= 1 bf16 ulp apart (ulp at max(|ref|, 2^-10));
+  both kernels round one fp32 result per element, and their fp32 paths differ only
+  in summation order and in rsqrt (the reference uses the hardware rsqrtf);
+* the text rows of the joint pack round twice (normalised -> bf16, then * w ->
+  bf16), so a 1-ulp flip of the normalised value is amplified by |w| (w ~ N(0, 1)
+  as in the reference test): <= 4 ulp, as against the oracle;
+* per-token FP8 quant: scales bit-equal on non-zero rows; the bytes may differ where
+  the reference's reciprocal multiply x * (1/s) and the IEEE division x / s of the
+  reference's PyTorch path (which this library follows) land on different sides of
+  an e4m3 rounding boundary: at most one code apart, on a tiny fraction of elements.
+  All-zero rows are the documented difference: the reference kernel writes scale 0,
+  the PyTorch path (and this library) 1e-8/448; both write zero bytes.
+"""
+from pathlib import Path
+
+import pytest
+import torch
+
+from conftest import assert_bf16_close, assert_ulp_close
+from oracle import ops
+
+REF_LIB = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "libjoyomni_ref.so"
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not REF_LIB.exists(), reason="oracle/_ref not built (no reference checkout)")]
+BF = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def ref(jo):
+    torch.ops.load_library(str(REF_LIB))
+    return torch.ops.joyomni_ref
+
+
+def rand(shape, seed, scale=1.0, mean=0.0, dt=BF, dev="cuda"):
+    g = torch.Generator().manual_seed(seed)
+    return (mean + scale * torch.randn(*shape, generator=g)).to(dt).to(dev)
+
+
+@pytest.mark.parametrize("M,N,dt", [(3600, 3072, BF), (512, 4096, BF), (67, 1000, torch.float16),
+                                    (33, 3072, torch.float32)])
+def test_rmsnorm_vs_reference_kernel(jo, ref, M, N, dt):
+    x = rand((M, N), 1, dt=dt)
+    w = rand((N,), 2, 0.02, 1.0, dt=dt)
+    ours, theirs = jo.rmsnorm(x, w, 1e-6), ref.rmsnorm(x, w, 1e-6)
+    # fp32 outputs keep the fp32 differences themselves (summation order, rsqrtf): a few fp32 ulps
+    assert_ulp_close(ours, theirs, 8.0 if dt == torch.float32 else 1.0, what=f"rmsnorm {dt}")
+
+
+@pytest.mark.parametrize("M,N,rows,norm,affine", [(10800, 3072, 1, 0, False), (512, 4096, 512, 0, False),
+                                                  (512, 4096, 1, 1, True), (300, 3072, 300, 0, True)])
+def test_norm_scale_shift_vs_reference_kernel(jo, ref, M, N, rows, norm, affine):
+    x = rand((M, N), 3)
+    scale, shift = rand((rows, N), 4, 0.1), rand((rows, N), 5, 0.1)
+    gamma = rand((N,), 6, 0.02, 1.0) if affine else None
+    beta = rand((N,), 7, 0.02) if affine and norm == 0 else None
+    ours = jo.fused_norm_scale_shift(x, gamma, beta, scale, shift, "layer" if norm == 0 else "rms", 1e-6)
+    theirs = ref.fused_norm_scale_shift(x, gamma, beta, scale, shift, norm, 1e-6)
+    assert_bf16_close(ours, theirs, 1.0, what="norm_scale_shift")
+
+
+@pytest.mark.parametrize("L,H", [(128, 8), (10800, 24)])
+def test_qk_norm_rope_vs_reference_kernel(jo, ref, L, H):
+    D = 128
+    q, k = rand((1, L * H, D), 8), rand((1, L * H, D), 9)
+    qw, kw = rand((D,), 10, 0.02, 1.0), rand((D,), 11, 0.02, 1.0)
+    if L == 10800:
+        (_, _), (cos, sin) = ops.rope_video_tables(3, 45, 80, 21)
+    else:
+        ang = torch.rand(L, D // 2, generator=torch.Generator().manual_seed(12)) * 6.28
+        cos, sin = ang.cos().to(BF), ang.sin().to(BF)
+    cos, sin = cos.cuda(), sin.cuda()
+    oq, ok, opre = q.clone(), k.clone(), torch.empty_like(k)
+    rq, rk, rpre = q.clone(), k.clone(), torch.empty_like(k)
+    jo.fused_qk_norm_rope_3d_paired(oq, ok, L, H, 1e-6, qw, kw, cos, sin, opre)
+    ref.fused_qk_norm_rope_3d_paired(rq, rk, L, H, 1e-6, qw, kw, cos, sin, rpre)
+    assert_bf16_close(oq, rq, 1.0, what="q")
+    assert_bf16_close(ok, rk, 1.0, what="k")
+    assert_bf16_close(opre, rpre, 1.0, what="k_pre_rope")
+
+
+@pytest.mark.parametrize("img,txt,cache,H", [(17, 11, 9, 4), (10800, 512, 43200, 24), (300, 64, 0, 24)])
+def test_joint_qkv_pack_vs_reference_kernel(jo, ref, img, txt, cache, H):
+    D = 128
+    # V (and Q/K) as strided unbind views of a [B, L, 3, H, D] projection, as the model passes them
+    iq, ik, iv = rand((1, img, 3, H, D), 13).unbind(2)
+    tq, tk, tv = rand((1, txt, 3, H, D), 14).unbind(2)
+    ck = rand((1, cache, H, D), 15) if cache else None
+    cv = rand((1, cache, H, D), 16) if cache else None
+    qw, kw = rand((D,), 17), rand((D,), 18)  # ~N(0, 1) as test_parity_light.py:147-148
+    oq, ok, ov = jo.fused_joint_qkv_pack(iq, ik, iv, tq, tk, tv, ck, cv, qw, kw, 1e-6)
+    rq, rk, rv = ref.fused_joint_qkv_pack(iq, ik, iv, tq, tk, tv, ck, cv, qw, kw, 1e-6)
+    assert torch.equal(ov, rv), "v"
+    assert torch.equal(oq[:, :img], rq[:, :img]), "image q rows"
+    assert torch.equal(ok[:, :cache + img], rk[:, :cache + img]), "cache and image k rows"
+    assert_bf16_close(oq[:, img:], rq[:, img:], 4.0, what="text q (double rounding)")
+    assert_bf16_close(ok[:, cache + img:], rk[:, cache + img:], 4.0, what="text k (double rounding)")
+
+
+@pytest.mark.parametrize("len0,len1,H", [(13, 7, 4), (4000, 1200, 24), (2000, 0, 24)])
+def test_cached_kv_pack_vs_reference_kernel(jo, ref, len0, len1, H):
+    D = 128
+    k0, v0 = rand((1, len0, H, D), 19), rand((1, len0, H, D), 20)
+    k1 = rand((1, len1, H, D), 21) if len1 else None
+    v1 = rand((1, len1, H, D), 22) if len1 else None
+    ang = torch.rand(len0 + len1, D // 2, generator=torch.Generator().manual_seed(23)) * 6.28
+    cos = ang.cos().repeat_interleave(2, dim=-1).contiguous().cuda()
+    sin = ang.sin().repeat_interleave(2, dim=-1).contiguous().cuda()
+    ok, ov = jo.fused_cached_kv_pack(k0, v0, k1, v1, cos, sin)
+    rk, rv = ref.fused_cached_kv_pack(k0, v0, k1, v1, cos, sin)
+    assert torch.equal(ov, rv), "v"
+    assert_bf16_close(ok, rk, 1.0, what="rotated k")
+
+
+@pytest.mark.parametrize("M,N,dt", [(10800, 3072, BF), (67, 4096, BF), (67, 4096, torch.float16)])
+def test_per_token_quant_vs_reference_kernel(jo, ref, M, N, dt):
+    x = rand((M, N), 24, dt=dt)
+    x[0].zero_()  # test_parity_light.py:117-119
+    x[1] *= 1e-3
+    qo = torch.empty(M, N, dtype=torch.float8_e4m3fn, device="cuda")
+    so = torch.empty(M, 1, dtype=torch.float32, device="cuda")
+    qr, sr = torch.empty_like(qo), torch.empty_like(so)
+    jo.sgl_per_token_quant_fp8(x, qo, so)
+    ref.sgl_per_token_quant_fp8(x, qr, sr)
+    # all-zero row: the documented difference of scale, identical (zero) bytes
+    assert sr[0].item() == 0.0 and so[0].item() == pytest.approx(1e-8 / 448, rel=1e-6)
+    assert torch.equal(qo[0].view(torch.uint8), qr[0].view(torch.uint8))
+    assert torch.equal(so[1:], sr[1:]), "scales of non-zero rows"
+    bo, br = qo[1:].view(torch.uint8).int(), qr[1:].view(torch.uint8).int()
+    differ = bo != br
+    frac = differ.float().mean().item()
+    assert frac < 1e-3, f"{frac:.2e} of the bytes differ"
+    if differ.any():  # same sign, neighbouring magnitude codes
+        assert torch.equal(bo[differ] & 0x80, br[differ] & 0x80)
+        assert ((bo[differ] & 0x7F) - (br[differ] & 0x7F)).abs().max().item() <= 1
+    # dequantised agreement, the reference test's own criterion (test_parity_light.py:127-133)
+    dq_o = qo[1:].float() * so[1:]
+    dq_r = qr[1:].float() * sr[1:]
+    rel = ((dq_o - dq_r).abs().mean() / dq_r.abs().mean()).item()
+    assert rel < 1e-5
