@@ -262,6 +262,20 @@ JO_API int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void*
                            const void* b3, int64_t proj_dim, void* scratch, int64_t scratch_bytes,
                            float max_period, void* stream);
 
+/* jo_timestep_mlp with the ModulateWan table add folded into time_proj's
+ * epilogue: besides vec, writes mods[t, b, :] = bf16(tables[t, :] + vec[b, :])
+ * for every t < n_tables (vec rounded to bf16 first, as the module adds the bf16
+ * time_proj output).  One launch serves every block and stream of a forward:
+ * tables bf16 [n_tables, proj_dim] (each block's img_mod / txt_mod
+ * modulate_table, [6, D] flattened), mods bf16 [n_tables, batch, proj_dim].
+ * Replaces ModulateWan.forward (deploy/xvideo/models/dit/dit.py:103-116), one
+ * torch add per block and stream, after the timestep branch (dit.py:574-579,
+ * 605-620).  Other arguments as jo_timestep_mlp. */
+JO_API int jo_timestep_mlp_modulate(void* vec, void* mods, const void* tables, int64_t n_tables, const float* t,
+                                    int64_t batch, const void* w1, const void* b1, int64_t freq_dim, int64_t dim,
+                                    const void* w2, const void* b2, const void* w3, const void* b3, int64_t proj_dim,
+                                    void* scratch, int64_t scratch_bytes, float max_period, void* stream);
+
 /* jo_timestep_mlp without the scratch argument, for callers that cannot
  * allocate device memory.  No counterpart in the reference.  The two bf16
  * intermediates go to a file-scope device array of 256 KB, so

@@ -380,7 +380,8 @@ struct GroupRed {
 // does (fused_norm_scale_shift.cu:136,157): both move rstd by a few fp32 ulps.
 template <typename T, int kVPT, int kNorm, int kEpi, int kF>
 __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (&raw)[kVPT], int lane,
-                                          uint32_t cache, int nvec, float inv_n, const GroupRed& red) {
+                                          uint32_t cache, int nvec, float inv_n, const GroupRed& red,
+                                          uint64_t pol) {
   const int GT = red.G * 32;  // threads of the row group; this thread's vectors: lane + GT * i
   constexpr int V = Elt<T>::kVec, P = V / 2;
   constexpr bool k16 = V == 8;
@@ -469,7 +470,10 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
         for (int e = 0; e < P; ++e) y[e] = __ffma2_rn(y[e], c1[e], sh[e]);
       }
       if constexpr (kEpi == kStoreY) {
-        st_global(reinterpret_cast<T*>(a.out) + row * a.out_stride + (int64_t)idx * V, from_pairs<T>(y));
+        if constexpr (kRowHint > 1)
+          st_global_hint(reinterpret_cast<T*>(a.out) + row * a.out_stride + (int64_t)idx * V, from_pairs<T>(y), pol);
+        else
+          st_global(reinterpret_cast<T*>(a.out) + row * a.out_stride + (int64_t)idx * V, from_pairs<T>(y));
         continue;
       } else {
         raw[i] = from_pairs<T>(y);  // y rounded to T, as the unfused chain materialises it
@@ -514,7 +518,10 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
                             e4m3_signs(raw[i].x, raw[i].y);
         const uint32_t w1 = ((uint32_t)e4m3x2(q[2].x, q[2].y) | ((uint32_t)e4m3x2(q[3].x, q[3].y) << 16)) |
                             e4m3_signs(raw[i].z, raw[i].w);
-        *reinterpret_cast<uint2*>(qrow + (int64_t)idx * 8) = make_uint2(w0, w1);
+        if constexpr (kRowHint > 1)
+          st_global_hint8(qrow + (int64_t)idx * 8, make_uint2(w0, w1), pol);
+        else
+          *reinterpret_cast<uint2*>(qrow + (int64_t)idx * 8) = make_uint2(w0, w1);
       } else {
         const float2 q0 = div2_markstein(p[0], s2, rc2), q1 = div2_markstein(p[1], s2, rc2);
         *reinterpret_cast<uint32_t*>(qrow + (int64_t)idx * 4) =
@@ -538,6 +545,25 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
 // operands (gamma, beta, 1+scale, shift, gate) are staged once per CTA in
 // shared memory as fp32 sets.
 constexpr int kMaxWarps = 32;
+// Bytes of row slots per SM the staged launcher aims for (see launch_staged_f).
+// Measured on B200 (LN + modulate, quant, RMSNorm -> FP8 at [10800, 3072]):
+// 96 KB beats 144 and 180 KB by 5-12 %; more bytes in flight per SM only slowed
+// the stream down.
+#ifndef JO_ROW_INFLIGHT_SM
+#define JO_ROW_INFLIGHT_SM (96u * 1024u)
+#endif
+constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
+// L2 hints of the staged path: 1 = row loads evict-first (each byte is read
+// once), 2 = the output stores too.
+#ifndef JO_ROW_HINT
+#define JO_ROW_HINT 0
+#endif
+constexpr int kRowHint = JO_ROW_HINT;
+// Groups with at most three rows in all keep every one of them in flight from
+// the start (1), or refill one slot at a time like longer matrices (0).
+#ifndef JO_ROW_SMALL_ALL
+#define JO_ROW_SMALL_ALL 1
+#endif
 // threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread)
 constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : 512); }
 
@@ -583,6 +609,14 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   const uint32_t bar0 = base + 8u * (uint32_t)(grp * m);
   const uint32_t slot0 = base + cfg.data_off + (uint32_t)(grp * m) * cfg.slot_bytes;
   // unit k of this group is row r0 + grp + k * NG, in slot k % m, phase (k / m) & 1
+  uint64_t pol = 0;
+  if constexpr (kRowHint > 0) pol = policy_evict_first();
+  auto load = [&](uint32_t dst, const void* src, uint32_t bar) {
+    if constexpr (kRowHint > 0)
+      bulk_load_hint(dst, src, row_bytes, bar, pol);
+    else
+      bulk_load(dst, src, row_bytes, bar);
+  };
   auto issue = [&](int k) {
     const int i = grp + k * NG;
     if (i >= units) return;
@@ -590,11 +624,11 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
     const uint32_t bar = bar0 + 8u * (uint32_t)(k % m), dst = slot0 + (uint32_t)(k % m) * cfg.slot_bytes;
     if constexpr (kPro != kResidGate) {
       mbar_expect_tx(bar, row_bytes);
-      bulk_load(dst, reinterpret_cast<const T*>(a.x) + row * a.x_stride, row_bytes, bar);
+      load(dst, reinterpret_cast<const T*>(a.x) + row * a.x_stride, bar);
     } else {
       mbar_expect_tx(bar, 2 * row_bytes);
-      bulk_load(dst, reinterpret_cast<const T*>(a.x) + row * a.x_stride, row_bytes, bar);
-      bulk_load(dst + row_bytes, reinterpret_cast<const T*>(a.res) + row * a.res_stride, row_bytes, bar);
+      load(dst, reinterpret_cast<const T*>(a.x) + row * a.x_stride, bar);
+      load(dst + row_bytes, reinterpret_cast<const T*>(a.res) + row * a.res_stride, bar);
     }
   };
   if (leader)
@@ -648,7 +682,10 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
 #pragma unroll
             for (int e = 0; e < P; ++e) x[e] = __ffma2_rn(x[e], g[e], r[e]);
             raw[v] = from_pairs<T>(x);
-            st_global(reinterpret_cast<T*>(a.out_h) + row * a.h_stride + (int64_t)idx * V, raw[v]);
+            if constexpr (kRowHint > 1)
+              st_global_hint(reinterpret_cast<T*>(a.out_h) + row * a.h_stride + (int64_t)idx * V, raw[v], pol);
+            else
+              st_global(reinterpret_cast<T*>(a.out_h) + row * a.h_stride + (int64_t)idx * V, raw[v]);
           }
         }
       }
@@ -663,7 +700,7 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(k + m);
     }
-    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, gl, cache, nvec, inv_n, red);
+    if constexpr (kEpi != kNoY) row_math2<T, kVPT, kNorm, kEpi, kF>(a, row, raw, gl, cache, nvec, inv_n, red, pol);
   }
   // error path only (a wait expired at unit k): the copies the leader issued
   // for units k .. k+m-1 must land before the CTA exits
@@ -811,15 +848,27 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   const uint32_t cache_bytes = (uint32_t)(Sets<kF>::n * 4 * a.cols + 127) & ~127u;
   if (cache_bytes + 2048u >= kBudget) return fail(JO_ERR_SHAPE, "row kernel: rows too large to stage");
   const uint32_t avail = kBudget - cache_bytes - 2048u;
-  // ~6 KB in flight per group is enough to cover the load latency: one slot
-  // for 3072-wide bf16 rows, up to three for short rows
-  int ng = cfg.warps / cfg.G;
-  cfg.m = (int)((6144u + cfg.slot_bytes - 1) / cfg.slot_bytes);
+  // Slots: a group refills a slot as soon as it has pulled the row out of it,
+  // but while it computes, its landed rows wait and nothing else is in flight
+  // for it; so the SM keeps kRowInflightSm bytes of slots (m per group, at most
+  // 3), giving up a group (down to 3/4 of them) before it gives up a slot.
+  const int ng_max = cfg.warps / cfg.G;
+  int ng = ng_max;
+  cfg.m = (int)((kRowInflightSm + (uint32_t)ng * cfg.slot_bytes - 1) / ((uint32_t)ng * cfg.slot_bytes));
+  if (cfg.m < 1) cfg.m = 1;
   // a group with only 2-3 rows in all keeps all of them in flight from the start
   const int64_t group_rows = cdiv(cdiv(a.rows, (int64_t)di->sm_count), (int64_t)ng);
-  if (group_rows <= 3 && cfg.m < group_rows) cfg.m = (int)group_rows;
+  if (JO_ROW_SMALL_ALL && group_rows <= 3 && cfg.m < group_rows) cfg.m = (int)group_rows;
   if (cfg.m > 3) cfg.m = 3;
-  while (cfg.m > 1 && (uint32_t)(ng * cfg.m) * cfg.slot_bytes > avail) --cfg.m;
+  while ((uint32_t)(ng * cfg.m) * cfg.slot_bytes > avail) {
+    if (cfg.m > 1 && 4 * (ng - 1) < 3 * ng_max)
+      --cfg.m;
+    else if (ng > 1)
+      --ng;
+    else
+      break;
+  }
+  cfg.warps = ng * cfg.G;
   if ((uint32_t)ng * cfg.slot_bytes > avail) {  // fewer groups, one slot each
     ng = (int)(avail / cfg.slot_bytes);
     cfg.warps = ng * cfg.G;
@@ -832,9 +881,10 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   const size_t smem = cfg.data_off + (size_t)ng * cfg.m * cfg.slot_bytes;
   static std::atomic<uint64_t> reserved{0};
   if (int s = reserve_smem((const void*)kern, 220 * 1024, reserved, di, "row kernel")) return s;
-  int64_t grid = di->sm_count;
-  const int64_t min_rows = 2 * ng;  // at least two rows per group before adding CTAs
-  if (grid * min_rows > a.rows) grid = cdiv(a.rows, min_rows);
+  // one CTA per SM whenever every SM gets a row: a short matrix (3600 rows: ~25
+  // per SM) is spread over all SMs with each group's 1-3 rows in flight at once
+  // (m above), rather than packed into fewer CTAs that leave SMs idle
+  int64_t grid = a.rows < di->sm_count ? a.rows : di->sm_count;
   if (grid < 1) grid = 1;
   if (cudaError_t e = launch_pdl(kern, dim3((unsigned)grid), dim3(cfg.warps * 32), smem, st, a, cfg, di->fault))
     return launch_failed(e, "row kernel");

@@ -43,6 +43,11 @@ struct TembLayer {
   __nv_bfloat16* y;        // [B, N]
   int K, N, B;
   float neg_log_period;    // -ln(max_period) rounded to fp32
+  // time_proj only: ModulateWan tables [T, N] added to the rounded output,
+  // mods[t, b, n] = bf16(tables[t, n] + y[b, n]) (null / 0: none)
+  const __nv_bfloat16* tables;
+  __nv_bfloat16* mods;
+  int T;
 };
 
 struct TembCfg {
@@ -76,8 +81,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x < kWarps * m) mbar_init(base + 8u * threadIdx.x, 1);
   if (threadIdx.x == 0) mbar_init_fence();
   __syncthreads();
-  pdl_wait();  // the previous layer's output (our input) is complete from here on
-  pdl_trigger();
   const uint32_t bar0 = base + 8u * (uint32_t)(warp * m);
   const uint32_t slot0 = base + cfg.data_off + (uint32_t)(warp * m) * cfg.slot_bytes;
   auto unit_rows = [&](int u) { return min(R, nrows - u * R); };
@@ -90,7 +93,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_expect_tx(bar, bytes);
     bulk_load(slot0 + (uint32_t)(k % m) * cfg.slot_bytes, a.w + (r0 + (int64_t)u * R) * K, bytes, bar);
   };
-  if (lane == 0)
+  // Layers 2 and 3 follow a layer of this MLP, which never writes weights, and
+  // are launched only once that layer has passed its own wait (so every kernel
+  // before it has completed): their first weight copies go out before the wait
+  // and overlap the previous layer.  Layer 1 follows the caller's work and
+  // waits first.
+  constexpr bool kEarly = !kSinIn;
+  if (kEarly && lane == 0)
+    for (int k = 0; k < m; ++k) issue(k);
+  pdl_wait();  // the previous layer's output (our input) is complete from here on
+  pdl_trigger();
+  if (!kEarly && lane == 0)
     for (int k = 0; k < m; ++k) issue(k);
 
   // ---- stage the batch's input rows while the first weight rows are in flight
@@ -151,11 +164,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float bias = a.bias ? __bfloat162float(a.bias[n]) : 0.f;
 #pragma unroll
       for (int b = 0; b < kB; ++b) {
-        const float h = warp_sum(acc[b]) + bias;
+        const float h = warp_sum(acc[b]) + bias;  // every lane holds the sum
         if (lane == b && b0 + b < a.B) {
           float y = __bfloat162float(__float2bfloat16_rn(h));
           if constexpr (kSilu) y = silu_exact(y);
           a.y[(int64_t)(b0 + b) * a.N + n] = __float2bfloat16_rn(y);
+        }
+        if constexpr (!kSilu) {
+          if (a.T > 0 && b0 + b < a.B) {  // ModulateWan: bf16(table + bf16(vec)), tables spread over the lanes
+            const float y = __bfloat162float(__float2bfloat16_rn(h));
+            for (int t = lane; t < a.T; t += 32)
+              a.mods[((int64_t)t * a.B + b0 + b) * a.N + n] =
+                  __float2bfloat16_rn(__bfloat162float(a.tables[(int64_t)t * a.N + n]) + y);
+          }
         }
       }
     }
@@ -221,7 +242,7 @@ int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
 int timestep_mlp_run(void* vec, const float* t, int64_t batch, const void* w1, const void* b1,
                      int64_t freq_dim, int64_t dim, const void* w2, const void* b2, const void* w3,
                      const void* b3, int64_t proj_dim, __nv_bfloat16* scratch, float max_period,
-                     cudaStream_t st, const DeviceInfo* di) {
+                     cudaStream_t st, const DeviceInfo* di, const void* tables, void* mods, int64_t n_tables) {
   TembLayer l{};
   l.t = t;
   l.B = (int)batch;
@@ -251,6 +272,9 @@ int timestep_mlp_run(void* vec, const float* t, int64_t batch, const void* w1, c
   l.y = reinterpret_cast<__nv_bfloat16*>(vec);
   l.K = (int)dim;
   l.N = (int)proj_dim;
+  l.tables = reinterpret_cast<const __nv_bfloat16*>(tables);
+  l.mods = reinterpret_cast<__nv_bfloat16*>(mods);
+  l.T = (int)n_tables;
   return launch_layer<false, false>(l, st, di);
 }
 
@@ -289,7 +313,29 @@ int jo_timestep_mlp(void* vec, const float* t, int64_t batch, const void* w1, co
     return fail(JO_ERR_SHAPE, "timestep_mlp: scratch needs %lld bytes, got %lld", (long long)(4 * batch * dim),
                 (long long)scratch_bytes);
   return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
-                          reinterpret_cast<__nv_bfloat16*>(scratch), max_period, (cudaStream_t)stream, di);
+                          reinterpret_cast<__nv_bfloat16*>(scratch), max_period, (cudaStream_t)stream, di, nullptr,
+                          nullptr, 0);
+}
+
+int jo_timestep_mlp_modulate(void* vec, void* mods, const void* tables, int64_t n_tables, const float* t,
+                             int64_t batch, const void* w1, const void* b1, int64_t freq_dim, int64_t dim,
+                             const void* w2, const void* b2, const void* w3, const void* b3, int64_t proj_dim,
+                             void* scratch, int64_t scratch_bytes, float max_period, void* stream) {
+  const char* op = "timestep_mlp_modulate";
+  const DeviceInfo* di;
+  if (int s = device_info(&di)) return s;
+  if (int s = timestep_mlp_check(vec, t, batch, w1, freq_dim, dim, w2, w3, proj_dim, max_period)) return s;
+  if (n_tables < 0 || n_tables > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: bad table count", op);
+  if (n_tables > 0 && (!tables || !mods)) return fail(JO_ERR_INVALID, "%s: null tables / mods", op);
+  if (n_tables * batch * proj_dim > INT64_MAX / 2) return fail(JO_ERR_SHAPE, "%s: output too large", op);
+  if (batch == 0) return JO_OK;
+  if (!scratch || !aligned16(scratch)) return fail(JO_ERR_ALIGN, "%s: scratch must be 16-byte aligned", op);
+  if (scratch_bytes < 4 * batch * dim)
+    return fail(JO_ERR_SHAPE, "%s: scratch needs %lld bytes, got %lld", op, (long long)(4 * batch * dim),
+                (long long)scratch_bytes);
+  return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
+                          reinterpret_cast<__nv_bfloat16*>(scratch), max_period, (cudaStream_t)stream, di, tables,
+                          mods, n_tables);
 }
 
 // ---------------------------------------------------------------------------
@@ -315,7 +361,7 @@ int jo_timestep_mlp_noalloc(void* vec, const float* t, int64_t batch, const void
   if (int s = symbol_address(cache, g_temb_scratch, di->ordinal, (cudaStream_t)stream, &ptr, "timestep_mlp_noalloc"))
     return s;
   return timestep_mlp_run(vec, t, batch, w1, b1, freq_dim, dim, w2, b2, w3, b3, proj_dim,
-                          reinterpret_cast<__nv_bfloat16*>(ptr), max_period, (cudaStream_t)stream, di);
+                          reinterpret_cast<__nv_bfloat16*>(ptr), max_period, (cudaStream_t)stream, di, nullptr, nullptr, 0);
 }
 
 }  // extern "C"

@@ -737,6 +737,49 @@ std::tuple<torch::Tensor, torch::Tensor> timestep_mlp(const torch::Tensor& t, co
   return std::make_tuple(vec, scratch[1]);
 }
 
+// timestep_mlp + every block's ModulateWan add in time_proj's epilogue:
+// returns (vec [B, proj_dim], mods [T, B, proj_dim]) for tables [T, proj_dim].
+std::tuple<torch::Tensor, torch::Tensor> timestep_mlp_modulate(const torch::Tensor& t, const torch::Tensor& w1,
+                                                               const c10::optional<torch::Tensor>& b1,
+                                                               const torch::Tensor& w2,
+                                                               const c10::optional<torch::Tensor>& b2,
+                                                               const torch::Tensor& w3,
+                                                               const c10::optional<torch::Tensor>& b3,
+                                                               const torch::Tensor& tables, double max_period) {
+  JO_CHECK_CUDA(t);
+  TORCH_CHECK(t.dim() == 1, "timesteps must be 1D");
+  for (const torch::Tensor* w : {&w1, &w2, &w3})
+    TORCH_CHECK(w->dim() == 2 && w->is_contiguous() && w->scalar_type() == torch::kBFloat16 &&
+                    w->device() == t.device(),
+                "weights must be contiguous bf16 [out, in] on the timesteps' device");
+  const int64_t dim = w1.size(0), freq = w1.size(1), proj = w3.size(0);
+  TORCH_CHECK(w2.size(0) == dim && w2.size(1) == dim && w3.size(1) == dim, "weight shapes do not chain");
+  check_dev(tables, t, "tables");
+  TORCH_CHECK(tables.is_contiguous() && tables.scalar_type() == torch::kBFloat16 && tables.numel() % proj == 0,
+              "tables must be contiguous bf16 [T, proj_dim]");
+  auto bias_ptr = [&](const c10::optional<torch::Tensor>& b, int64_t n) -> const void* {
+    if (!b.has_value()) return nullptr;
+    TORCH_CHECK(b->dim() == 1 && b->numel() == n && b->is_contiguous() && b->scalar_type() == torch::kBFloat16 &&
+                    b->device() == t.device(),
+                "bias must be contiguous bf16 [out] on the timesteps' device");
+    return b->data_ptr();
+  };
+  const void* pb1 = bias_ptr(b1, dim);
+  const void* pb2 = bias_ptr(b2, dim);
+  const void* pb3 = bias_ptr(b3, proj);
+  auto tf = t.to(torch::kFloat32).contiguous();
+  const c10::cuda::CUDAGuard guard(t.device());
+  const int64_t B = t.size(0), T = tables.numel() / proj;
+  auto vec = torch::empty({B, proj}, w1.options());
+  auto mods = torch::empty({T, B, proj}, w1.options());
+  auto scratch = torch::empty({2, B, dim}, w1.options());
+  jo_check(jo_timestep_mlp_modulate(vec.data_ptr(), mods.data_ptr(), tables.data_ptr(), T, tf.data_ptr<float>(), B,
+                                    w1.data_ptr(), pb1, freq, dim, w2.data_ptr(), pb2, w3.data_ptr(), pb3, proj,
+                                    scratch.data_ptr(), scratch.numel() * 2, (float)max_period, stream_of(t)),
+           "timestep_mlp_modulate");
+  return std::make_tuple(vec, mods);
+}
+
 std::tuple<torch::Tensor, torch::Tensor> rmsnorm_quant_fp8(const torch::Tensor& x, const torch::Tensor& weight,
                                                            double eps) {
   JO_CHECK_CUDA(x);
@@ -826,6 +869,9 @@ TORCH_LIBRARY(joyomni_ops, m) {
   m.def(
       "timestep_mlp(Tensor t, Tensor w1, Tensor? b1, Tensor w2, Tensor? b2, Tensor w3, Tensor? b3, "
       "float max_period) -> (Tensor, Tensor)");
+  m.def(
+      "timestep_mlp_modulate(Tensor t, Tensor w1, Tensor? b1, Tensor w2, Tensor? b2, Tensor w3, Tensor? b3, "
+      "Tensor tables, float max_period) -> (Tensor, Tensor)");
   m.def("rmsnorm_quant_fp8(Tensor x, Tensor weight, float eps) -> (Tensor, Tensor)");
   m.def(
       "norm_scale_shift_quant_fp8(Tensor x, Tensor? gamma, Tensor? beta, Tensor scale, Tensor shift, "
@@ -852,6 +898,7 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("silu_mul", &silu_mul);
   m.impl("timestep_embedding", &timestep_embedding);
   m.impl("timestep_mlp", &timestep_mlp);
+  m.impl("timestep_mlp_modulate", &timestep_mlp_modulate);
   m.impl("rmsnorm_quant_fp8", &rmsnorm_quant_fp8);
   m.impl("norm_scale_shift_quant_fp8", &norm_scale_shift_quant_fp8);
 }

@@ -45,6 +45,7 @@ __all__ = [
     "silu_mul",
     "timestep_embedding",
     "timestep_mlp",
+    "timestep_mlp_modulate",
     "fp8_scaled_mm_gated_residual",
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
@@ -177,6 +178,13 @@ def _fake_fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dty
 @torch.library.register_fake("joyomni_ops::timestep_mlp")
 def _fake_timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period):
     return (w1.new_empty((t.shape[0], w3.shape[0])), w1.new_empty((t.shape[0], w1.shape[0])))
+
+
+@torch.library.register_fake("joyomni_ops::timestep_mlp_modulate")
+def _fake_timestep_mlp_modulate(t, w1, b1, w2, b2, w3, b3, tables, max_period):
+    proj = w3.shape[0]
+    n_tables = tables.numel() // proj
+    return w1.new_empty((t.shape[0], proj)), w1.new_empty((n_tables, t.shape[0], proj))
 
 
 @torch.library.register_fake("joyomni_ops::rmsnorm_quant_fp8")
@@ -317,6 +325,13 @@ def timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period=10000.0):
     sinusoid(t) -> linear_1 -> SiLU -> linear_2 -> SiLU -> time_proj.
     Returns (vec bf16 [B, proj_dim], silu(temb) bf16 [B, dim])."""
     return _ops.timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period)
+
+
+def timestep_mlp_modulate(t, w1, b1, w2, b2, w3, b3, tables, max_period=10000.0):
+    """timestep_mlp plus every block's ModulateWan add (dit.py:103-116) in time_proj's epilogue.
+    tables: bf16 [T, proj_dim] (each block's and stream's modulate_table, [6, D] flattened).
+    Returns (vec bf16 [B, proj_dim], mods bf16 [T, B, proj_dim] = bf16(tables[t] + vec))."""
+    return _ops.timestep_mlp_modulate(t, w1, b1, w2, b2, w3, b3, tables.reshape(-1, w3.shape[0]), max_period)
 
 
 def rmsnorm_quant_fp8(x, weight, eps=1e-6):

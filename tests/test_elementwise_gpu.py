@@ -81,6 +81,20 @@ def test_timestep_embedding(jo, dev, flip, dim, shift):
     t[1] = 999.0
     out = jo.timestep_embedding(t.to(dev), dim, flip, shift, 1.0, 10000.0)
     ref = ops.timestep_embedding(t, dim, flip, shift, 1.0, 10000.0)
-    assert (out.cpu() - ref).abs().max().item() <= 2e-4
+    # Error bound, elementwise.  The exponent (-ln P * i) / (half - shift) is the same
+    # IEEE fp32 product and quotient on both sides; exp differs by <= 2 + 1 ulp (CUDA expf,
+    # the CPU's exp), so f = exp(.) by <= 3 * 2^-24 relative, and the argument t * f (one
+    # more rounding each) by <= |t f| * 2^-22; sin / cos add <= 2 + 1 ulp of a value in
+    # [-1, 1] (<= 3 * 2^-24) and move by at most the argument's change.  Asserted with a
+    # factor-2 margin: |diff| <= |t f| * 2^-21 + 2^-21.
+    half = dim // 2
+    f = torch.exp(-torch.log(torch.tensor(10000.0)) * torch.arange(half, dtype=torch.float32) / (half - shift))
+    arg = (t[:, None] * f[None, :]).abs()
+    bound = arg * 2.0 ** -21 + 2.0 ** -21
+    bound = torch.cat([bound, bound], dim=1)
+    if dim % 2:
+        bound = torch.nn.functional.pad(bound, (0, 1))
+    diff = (out.cpu() - ref).abs()
+    assert (diff <= bound).all(), f"max excess {(diff - bound).max().item():.3e}"
     # frequency 0 is exact: cos(t) / sin(t) of the timestep itself
     assert (out.cpu()[:, 0 if flip else dim // 2] - torch.cos(t)).abs().max().item() <= 1e-6

@@ -17,7 +17,9 @@ at the reference tests' own shapes (joyomni_ops/tests/test_parity_light.py):
 * per-token FP8 quant: scales bit-equal on non-zero rows; the bytes may differ where
   the reference's reciprocal multiply x * (1/s) and the IEEE division x / s of the
   reference's PyTorch path (which this library follows) land on different sides of
-  an e4m3 rounding boundary: at most one code apart, on a tiny fraction of elements.
+  an e4m3 rounding boundary: at most one code apart, on a tiny fraction of elements,
+  and only where the exact quotient is a rounding tie (frequent with bf16 inputs,
+  whose ratios x * 448 / amax often hit a midpoint exactly).
   All-zero rows are the documented difference: the reference kernel writes scale 0,
   the PyTorch path (and this library) 1e-8/448; both write zero bytes.
 """
@@ -135,15 +137,30 @@ def test_per_token_quant_vs_reference_kernel(jo, ref, M, N, dt):
     assert sr[0].item() == 0.0 and so[0].item() == pytest.approx(1e-8 / 448, rel=1e-6)
     assert torch.equal(qo[0].view(torch.uint8), qr[0].view(torch.uint8))
     assert torch.equal(so[1:], sr[1:]), "scales of non-zero rows"
+    # ours is the reference's PyTorch path bit for bit (fp8_linear.py:38-43)
+    q_pt, s_pt = ops.per_token_quant_fp8(x.cpu())
+    assert torch.equal(qo.cpu().view(torch.uint8), q_pt.view(torch.uint8)) and torch.equal(so.cpu(), s_pt)
     bo, br = qo[1:].view(torch.uint8).int(), qr[1:].view(torch.uint8).int()
     differ = bo != br
     frac = differ.float().mean().item()
     assert frac < 1e-3, f"{frac:.2e} of the bytes differ"
-    if differ.any():  # same sign, neighbouring magnitude codes
+    if differ.any():
+        # same sign, neighbouring magnitude codes, and every difference is a rounding
+        # (near-)tie: the exact quotient x / s lies on the midpoint of the two codes,
+        # where the reference kernel's x * (1/s) (two roundings) and the IEEE division
+        # land on different sides
         assert torch.equal(bo[differ] & 0x80, br[differ] & 0x80)
         assert ((bo[differ] & 0x7F) - (br[differ] & 0x7F)).abs().max().item() <= 1
-    # dequantised agreement, the reference test's own criterion (test_parity_light.py:127-133)
+        rows = differ.nonzero()[:, 0] + 1
+        exact = x[1:][differ].double() / so[rows, 0].double()
+        a, b = qo[1:][differ].float().double(), qr[1:][differ].float().double()
+        mid = (a + b) / 2
+        assert ((exact - mid).abs() <= mid.abs() * 2.0 ** -20).all(), "a byte differs away from a rounding tie"
+    # dequantised agreement (the reference test's measure, test_parity_light.py:127-133): the
+    # tie-breaking differences above are one e4m3 step (<= 2^-3 relative) on < 1e-3 of the
+    # elements, so the mean relative difference is below 2^-3 * 1e-3.  (On bf16 N(0,1) data the
+    # reference kernel sits at ~2e-5 from the PyTorch path, above that test's own 1e-5 gate.)
     dq_o = qo[1:].float() * so[1:]
     dq_r = qr[1:].float() * sr[1:]
     rel = ((dq_o - dq_r).abs().mean() / dq_r.abs().mean()).item()
-    assert rel < 1e-5
+    assert rel < 2.0 ** -3 * 1e-3

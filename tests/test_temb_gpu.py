@@ -89,3 +89,22 @@ def test_timestep_mlp_rejects(dev):
                         small.data_ptr(), 200, 10000.0, cabi.stream())
     assert st == cabi.JO_ERR_SHAPE
     assert "scratch" in cabi.last_error()
+
+
+@pytest.mark.parametrize("B,n_tables", [(1, 80), (2, 3), (1, 0)])
+def test_timestep_mlp_modulate(jo, dev, B, n_tables):
+    """The ModulateWan add (dit.py:103-116: modulate_table + vec in bf16) folded into
+    time_proj's epilogue: vec equals the plain MLP's bit for bit, and every block's
+    modulation rows equal bf16(table + vec) bit for bit."""
+    D = 3072
+    t = (torch.rand(B, generator=torch.Generator().manual_seed(40 + B)) * 1000.0).to(dev)
+    ws = [None if x is None else x.to(dev) for x in weights(256, D, 6 * D, 41)]
+    g = torch.Generator().manual_seed(42)
+    tables = (torch.randn(n_tables, 6, D, generator=g) / D ** 0.5).to(BF).to(dev)
+    vec, mods = jo.timestep_mlp_modulate(t, *ws, tables)
+    want_vec, _ = jo.timestep_mlp(t, *ws)
+    assert torch.equal(vec, want_vec)
+    assert mods.shape == (n_tables, B, 6 * D)
+    # the module's own arithmetic on the bf16 time_proj output (dit.py:115)
+    want = tables.view(n_tables, 1, 6 * D) + vec.view(1, B, 6 * D)
+    assert torch.equal(mods, want)
