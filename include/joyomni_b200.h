@@ -117,6 +117,8 @@ JO_API int jo_joint_qkv_pack(void* out_q, void* out_k, void* out_v, jo_view4 img
 /* fused_cached_kv_pack: concatenates one or two pre-RoPE K/V segments into
  * contiguous bf16 [1, len0+len1, heads, 128] and applies interleaved RoPE to K
  * with fp32 full-width cos/sin [len0+len1, 128].  key1.ptr == NULL: one segment.
+ * value0.ptr == NULL (with out_value and value1.ptr NULL): keys only, no values
+ * copied (the rotation of a cache whose values stay where they are).
  * Replaces joyomni_ops::fused_cached_kv_pack
  * (joyomni_ops/csrc/fused_joint_qkv_pack.cu:344-415). */
 JO_API int jo_cached_kv_pack(void* out_key, void* out_value, jo_view4 key0, jo_view4 value0,
@@ -208,6 +210,22 @@ JO_API int jo_qkv_norm_rope_pack_host(void* host_q, void* host_k, void* host_v, 
                                       const void* q_weight, const void* k_weight, const void* cos, const void* sin,
                                       float eps, int64_t chunk_tokens, void* stream, void* h2d_stream,
                                       void* d2h_stream);
+
+/* Merge of two partial attention outputs over disjoint key sets A and B by
+ * their log-sum-exps: per (row s, head h), m = max(lA, lB),
+ * out = (e^(lA-m) oA + e^(lB-m) oB) / (e^(lA-m) + e^(lB-m)), fp32 math, one
+ * rounding.  oA/oB/out: bf16 or fp16 [rows, heads, head_dim] views, element
+ * (s, h, d) at p[s*stride_s + h*stride_h + d]; lse_a/lse_b: fp32 natural-log
+ * log-sum-exps of the scaled scores, element (h, s) at p[h*stride_h + s*stride_s].
+ * Attention over [cache | chunk | text] keys (deploy/xvideo/models/dit/dit.py:
+ * 154-189, 498) is the merge of the attention over the cache rows and over the
+ * rest, so the cache part can run while the chunk's K/V are still being
+ * gathered from the other ranks.  No single reference kernel. */
+JO_API int jo_attn_merge(void* out, int64_t out_stride_s, int64_t out_stride_h, const void* o_a, int64_t a_stride_s,
+                         int64_t a_stride_h, const float* lse_a, int64_t lse_a_stride_h, int64_t lse_a_stride_s,
+                         const void* o_b, int64_t b_stride_s, int64_t b_stride_h, const float* lse_b,
+                         int64_t lse_b_stride_h, int64_t lse_b_stride_s, int64_t rows, int64_t heads,
+                         int64_t head_dim, int dtype, void* stream);
 
 /* gated residual: out = residual + x * gate (fp32 math, one rounding); gate is
  * [gate_rows, cols] with gate_rows in {1, rows}.

@@ -858,24 +858,28 @@ int jo_cached_kv_pack(void* out_key, void* out_value, jo_view4 key0, jo_view4 va
   const DeviceInfo* di;
   if (int s = device_info(&di)) return s;
   if (heads <= 0 || key0.len <= 0) return fail(JO_ERR_SHAPE, "%s: cache length and heads must be positive", op);
-  if (value0.len != key0.len) return fail(JO_ERR_SHAPE, "%s: key0/value0 lengths must match", op);
+  // K only (value0.ptr == out_value == NULL): rotate the keys, copy no values
+  const bool has_v = value0.ptr != nullptr;
+  if (!has_v && (out_value != nullptr || value1.ptr != nullptr))
+    return fail(JO_ERR_INVALID, "%s: without value0, out_value and value1 must be null too", op);
+  if (has_v && value0.len != key0.len) return fail(JO_ERR_SHAPE, "%s: key0/value0 lengths must match", op);
   const bool two = key1.ptr != nullptr;
-  if (two != (value1.ptr != nullptr))
+  if (has_v && two != (value1.ptr != nullptr))
     return fail(JO_ERR_INVALID, "%s: key1 and value1 must both be present or absent", op);
-  if (two && (key1.len <= 0 || value1.len != key1.len))
+  if (two && (key1.len <= 0 || (has_v && value1.len != key1.len)))
     return fail(JO_ERR_SHAPE, "%s: key1/value1 lengths must match and be positive", op);
-  if (!out_key || !out_value || !key0.ptr || !value0.ptr || !cos || !sin)
+  if (!out_key || (has_v && !out_value) || !key0.ptr || !cos || !sin)
     return fail(JO_ERR_INVALID, "%s: null operand", op);
   const int64_t len1 = two ? key1.len : 0;
   const int64_t total = (key0.len + len1) * heads;
   if (2 * total > (int64_t)INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many rows", op);
-  if (!aligned16(out_key) || !aligned16(out_value) || !aligned16(cos) || !aligned16(sin))
+  if (!aligned16(out_key) || (has_v && !aligned16(out_value)) || !aligned16(cos) || !aligned16(sin))
     return fail(JO_ERR_ALIGN, "%s: outputs and cos/sin must be 16-byte aligned", op);
   CachedArgs a{};
   a.k0 = to_view(key0);
-  a.v0 = to_view(value0);
+  a.v0 = has_v ? to_view(value0) : View{nullptr, 0, 0};
   a.k1 = two ? to_view(key1) : View{nullptr, 0, 0};
-  a.v1 = two ? to_view(value1) : View{nullptr, 0, 0};
+  a.v1 = two && has_v ? to_view(value1) : View{nullptr, 0, 0};
   a.cos = cos;
   a.sin = sin;
   a.ok = reinterpret_cast<__nv_bfloat16*>(out_key);
@@ -883,9 +887,9 @@ int jo_cached_kv_pack(void* out_key, void* out_value, jo_view4 key0, jo_view4 va
   a.heads = (uint32_t)heads;
   a.rows0 = (uint32_t)(key0.len * heads);
   a.total_rows = (uint32_t)total;
-  a.all_rows = (uint32_t)(2 * total);
-  bool vec = view_aligned(key0) && view_aligned(value0);
-  if (two) vec = vec && view_aligned(key1) && view_aligned(value1);
+  a.all_rows = (uint32_t)(has_v ? 2 * total : total);
+  bool vec = view_aligned(key0) && (!has_v || view_aligned(value0));
+  if (two) vec = vec && view_aligned(key1) && (!has_v || view_aligned(value1));
   cudaStream_t st = (cudaStream_t)stream;
   return vec ? launch_grid(cached_pack_kernel<true>, a, a.all_rows, st, di, "cached_pack_kernel")
              : launch_grid(cached_pack_kernel<false>, a, a.all_rows, st, di, "cached_pack_kernel");

@@ -26,6 +26,13 @@
 namespace jo {
 namespace rows {
 
+// L2 hints of the staged path: 1 = row loads evict-first (each byte is read
+// once), 2 = the output stores too.
+#ifndef JO_ROW_HINT
+#define JO_ROW_HINT 0
+#endif
+constexpr int kRowHint = JO_ROW_HINT;
+
 // Reduction over the threads that own one row.
 template <bool kWarp>
 __device__ __forceinline__ float row_reduce_sum(float v, float* smem) {
@@ -553,16 +560,16 @@ constexpr int kMaxWarps = 32;
 #define JO_ROW_INFLIGHT_SM (96u * 1024u)
 #endif
 constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
-// L2 hints of the staged path: 1 = row loads evict-first (each byte is read
-// once), 2 = the output stores too.
-#ifndef JO_ROW_HINT
-#define JO_ROW_HINT 0
-#endif
-constexpr int kRowHint = JO_ROW_HINT;
 // Groups with at most three rows in all keep every one of them in flight from
 // the start (1), or refill one slot at a time like longer matrices (0).
 #ifndef JO_ROW_SMALL_ALL
 #define JO_ROW_SMALL_ALL 1
+#endif
+// Rows of more than 128 vectors split over two warps (half the vectors per
+// thread, twice the warps per SM) for: 0 = residual rows only, 1 = also rows
+// with a quantising epilogue, 2 = also every normalising op.
+#ifndef JO_ROW_G2
+#define JO_ROW_G2 0
 #endif
 // threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread)
 constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : 512); }
@@ -841,7 +848,7 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   // one warp per row, except two-input rows (residual + x), whose row groups
   // of G warps hold at most kVPT vectors per thread; warps per CTA by the
   // register budget (30 for G = 2: named barriers 1..15 name the groups)
-  cfg.G = kPro != kResidGate || nvec <= 32 * kVPT ? 1 : (nvec <= 64 * kVPT ? 2 : 4);
+  cfg.G = nvec <= 32 * kVPT ? 1 : (nvec <= 64 * kVPT ? 2 : 4);
   if (cfg.G * 32 * kVPT < nvec) return fail(JO_ERR_SHAPE, "row kernel: row group too small");
   cfg.warps = staged_threads(kVPT) / 32;
   if (cfg.G == 2 && cfg.warps > 30) cfg.warps = 30;
@@ -942,7 +949,9 @@ int launch_rows_t(const RowArgs& a, cudaStream_t st) {
 #define JO_STAGED(VPT) return launch_staged<T, VPT, kNorm, kPro, kEpi>(a, st, di)
       // vectors per thread: one warp per row, or (residual + x rows) the
       // smallest row group G in {1, 2, 4} with at most 4 vectors per thread
-      const int G = kPro != kResidGate || nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
+      const bool split = kPro == kResidGate || (JO_ROW_G2 >= 1 && kEpi == kQuantY && kNorm != kNoNorm) ||
+                         (JO_ROW_G2 >= 2 && kNorm != kNoNorm);
+      const int G = !split || nvec <= 128 ? 1 : (kPro != kResidGate || nvec <= 256 ? 2 : 4);
       const int vpt = (nvec + 32 * G - 1) / (32 * G);
       if (vpt <= 2) JO_STAGED(2);
       if (vpt <= 3) JO_STAGED(3);

@@ -301,6 +301,29 @@ std::tuple<torch::Tensor, torch::Tensor> fused_cached_kv_pack(const torch::Tenso
   return std::make_tuple(out_key, out_value);
 }
 
+// Rotation of pre-RoPE cached keys [L, H, 128] (any row / head strides) into a
+// contiguous [L, H, 128] buffer with fp32 full-width tables [L, 128]: the keys of
+// fused_cached_kv_pack (fused_joint_qkv_pack.cu:166-220) without the value copy.
+void cached_k_rotate_into(const torch::Tensor& key, const torch::Tensor& cos, const torch::Tensor& sin,
+                          torch::Tensor& out_key) {
+  JO_CHECK_CUDA(key);
+  check_dev(cos, key, "cos");
+  check_dev(sin, key, "sin");
+  check_dev(out_key, key, "out_key");
+  TORCH_CHECK(key.dim() == 3 && key.size(2) == 128 && key.stride(2) == 1, "key must be [L, H, 128]");
+  JO_CHECK_DTYPE(key, torch::kBFloat16);
+  JO_CHECK_INPUT(out_key, torch::kBFloat16);
+  TORCH_CHECK(out_key.sizes() == key.sizes(), "out_key must have key's shape");
+  JO_CHECK_INPUT(cos, torch::kFloat32);
+  JO_CHECK_INPUT(sin, torch::kFloat32);
+  TORCH_CHECK(cos.numel() == key.size(0) * 128 && sin.sizes() == cos.sizes(), "cos/sin must be [L, 128]");
+  const c10::cuda::CUDAGuard guard(key.device());
+  jo_view4 k0{key.data_ptr(), key.size(0), key.stride(0), key.stride(1)};
+  jo_check(jo_cached_kv_pack(out_key.data_ptr(), nullptr, k0, no_view(), no_view(), no_view(), cos.data_ptr<float>(),
+                             sin.data_ptr<float>(), key.size(1), stream_of(key)),
+           "cached_k_rotate_into");
+}
+
 // joyomni_ops/csrc/per_token_quant_fp8.cu:148-176
 void sgl_per_token_quant_fp8(torch::Tensor input, torch::Tensor output_q, torch::Tensor output_s) {
   JO_CHECK_CUDA(input);
@@ -496,8 +519,19 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> qkv_norm_rope_pack(
 void qkv_norm_rope_pack_into(const torch::Tensor& qkv, int64_t num_heads, const torch::Tensor& q_weight,
                              const torch::Tensor& k_weight, const c10::optional<torch::Tensor>& cos,
                              const c10::optional<torch::Tensor>& sin, double eps, torch::Tensor& q_out,
-                             torch::Tensor& k_out, torch::Tensor& v_out) {
+                             torch::Tensor& k_out, torch::Tensor& v_out,
+                             const c10::optional<torch::Tensor>& k_pre_out) {
   const auto [L, D] = check_qkv_pack(qkv, num_heads, q_weight, k_weight, cos, sin);
+  void* pre = nullptr;
+  if (k_pre_out.has_value() && k_pre_out->defined()) {
+    const torch::Tensor& p = *k_pre_out;
+    check_dev(p, qkv, "k_pre_out");
+    JO_CHECK_DTYPE(p, torch::kBFloat16);
+    TORCH_CHECK(p.dim() == 3 && p.size(0) == L && p.size(1) == num_heads && p.size(2) == D && p.stride(2) == 1 &&
+                    p.stride(0) == q_out.stride(0) && p.stride(1) == q_out.stride(1),
+                "k_pre_out must be a [tokens, heads, head_dim] view with the outputs' strides");
+    pre = p.data_ptr();
+  }
   for (const torch::Tensor* t : {&q_out, &k_out, &v_out}) {
     JO_CHECK_CUDA(*t);
     check_dev(*t, qkv, "q/k/v output");
@@ -508,7 +542,7 @@ void qkv_norm_rope_pack_into(const torch::Tensor& qkv, int64_t num_heads, const 
                 "q/k/v outputs must share token and head strides with a contiguous last dim");
   }
   const c10::cuda::CUDAGuard guard(qkv.device());
-  jo_check(jo_qkv_norm_rope_pack(q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), nullptr, q_out.stride(1),
+  jo_check(jo_qkv_norm_rope_pack(q_out.data_ptr(), k_out.data_ptr(), v_out.data_ptr(), pre, q_out.stride(1),
                                  q_out.stride(0), qkv.data_ptr(), qkv.stride(0), L, num_heads, D, q_weight.data_ptr(),
                                  k_weight.data_ptr(), opt_ptr(cos), opt_ptr(sin), (float)eps, stream_of(qkv)),
            "qkv_norm_rope_pack_into");
@@ -563,6 +597,32 @@ void qkv_norm_rope_pack_host(const torch::Tensor& qkv_host, int64_t num_heads, c
                                       opt_ptr(cos), opt_ptr(sin), (float)eps, chunk_tokens, stream_of(q_weight),
                                       (void*)in.stream(), (void*)out.stream()),
            "qkv_norm_rope_pack_host");
+}
+
+// Partial attention outputs o_a / o_b [1, H, S, D] (any row / head strides, as
+// SDPA returns them) with their log-sum-exps [1, H, S] -> merged [S, H, D].
+torch::Tensor attn_merge(const torch::Tensor& o_a, const torch::Tensor& lse_a, const torch::Tensor& o_b,
+                         const torch::Tensor& lse_b) {
+  JO_CHECK_CUDA(o_a);
+  check_dev(o_b, o_a, "o_b");
+  check_dev(lse_a, o_a, "lse_a");
+  check_dev(lse_b, o_a, "lse_b");
+  TORCH_CHECK(o_a.dim() == 4 && o_a.size(0) == 1 && o_b.sizes() == o_a.sizes(), "o_a / o_b must be [1, H, S, D]");
+  TORCH_CHECK(o_a.stride(3) == 1 && o_b.stride(3) == 1, "o_a / o_b last dim must be contiguous");
+  TORCH_CHECK(o_a.scalar_type() == o_b.scalar_type(), "o_a / o_b dtypes must match");
+  const int64_t H = o_a.size(1), S = o_a.size(2), D = o_a.size(3);
+  for (const torch::Tensor* l : {&lse_a, &lse_b})
+    TORCH_CHECK(l->dim() == 3 && l->size(0) == 1 && l->size(1) == H && l->size(2) == S &&
+                    l->scalar_type() == torch::kFloat32,
+                "lse must be fp32 [1, H, S]");
+  const c10::cuda::CUDAGuard guard(o_a.device());
+  auto out = torch::empty({S, H, D}, o_a.options());
+  jo_check(jo_attn_merge(out.data_ptr(), H * D, D, o_a.data_ptr(), o_a.stride(2), o_a.stride(1),
+                         lse_a.data_ptr<float>(), lse_a.stride(1), lse_a.stride(2), o_b.data_ptr(), o_b.stride(2),
+                         o_b.stride(1), lse_b.data_ptr<float>(), lse_b.stride(1), lse_b.stride(2), S, H, D,
+                         dt_code(o_a.scalar_type()), stream_of(o_a)),
+           "attn_merge");
+  return out;
 }
 
 std::tuple<torch::Tensor, torch::Tensor> gelu_quant_fp8(const torch::Tensor& x) {
@@ -848,11 +908,14 @@ TORCH_LIBRARY(joyomni_ops, m) {
       "Tensor? sin, float eps, bool head_major, Tensor(a!)? k_pre_rope) -> (Tensor, Tensor, Tensor)");
   m.def(
       "qkv_norm_rope_pack_into(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
-      "Tensor? sin, float eps, Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out) -> ()");
+      "Tensor? sin, float eps, Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!)? k_pre_out=None) "
+      "-> ()");
   m.def(
       "qkv_norm_rope_pack_host(Tensor qkv_host, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
       "Tensor? sin, float eps, bool head_major, Tensor(a!) q_host, Tensor(b!) k_host, Tensor(c!) v_host, "
       "int chunk_tokens) -> ()");
+  m.def("attn_merge(Tensor o_a, Tensor lse_a, Tensor o_b, Tensor lse_b) -> Tensor");
+  m.def("cached_k_rotate_into(Tensor key, Tensor cos, Tensor sin, Tensor(a!) out_key) -> ()");
   m.def("gelu_quant_fp8(Tensor x) -> (Tensor, Tensor)");
   m.def(
       "gated_residual_norm_scale_shift_quant_fp8(Tensor residual, Tensor x, Tensor gate, Tensor? gamma, "
@@ -890,6 +953,8 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("qkv_norm_rope_pack", &qkv_norm_rope_pack);
   m.impl("qkv_norm_rope_pack_into", &qkv_norm_rope_pack_into);
   m.impl("qkv_norm_rope_pack_host", &qkv_norm_rope_pack_host);
+  m.impl("attn_merge", &attn_merge);
+  m.impl("cached_k_rotate_into", &cached_k_rotate_into);
   m.impl("gelu_quant_fp8", &gelu_quant_fp8);
   m.impl("gated_residual_norm_scale_shift_quant_fp8", &gated_residual_norm_scale_shift_quant_fp8);
   m.impl("gated_residual", &gated_residual);

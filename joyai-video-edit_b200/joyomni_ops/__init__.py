@@ -51,7 +51,9 @@ __all__ = [
     "norm_scale_shift_quant_fp8",
     "qkv_norm_rope_pack_into",
     "qkv_norm_rope_pack_host",
+    "cached_k_rotate_into",
     "gelu_quant_fp8",
+    "attn_merge",
     "gated_residual_norm_scale_shift_quant_fp8",
     "library_path",
 ]
@@ -121,7 +123,13 @@ def _fake_qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, 
 
 
 @torch.library.register_fake("joyomni_ops::qkv_norm_rope_pack_into")
-def _fake_qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out):
+def _fake_qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out,
+                                  k_pre_out=None):
+    return None
+
+
+@torch.library.register_fake("joyomni_ops::cached_k_rotate_into")
+def _fake_cached_k_rotate_into(key, cos, sin, out_key):
     return None
 
 
@@ -129,6 +137,12 @@ def _fake_qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, 
 def _fake_qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, eps, head_major, q_host, k_host,
                                   v_host, chunk_tokens):
     return None
+
+
+@torch.library.register_fake("joyomni_ops::attn_merge")
+def _fake_attn_merge(o_a, lse_a, o_b, lse_b):
+    _, h, s, d = o_a.shape
+    return o_a.new_empty((s, h, d))
 
 
 @torch.library.register_fake("joyomni_ops::gelu_quant_fp8")
@@ -260,9 +274,17 @@ def qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps=1e-6, h
     return _ops.qkv_norm_rope_pack(qkv, num_heads, q_weight, k_weight, cos, sin, eps, head_major, k_pre_rope)
 
 
-def qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, q_out, k_out, v_out, eps=1e-6):
-    """qkv_norm_rope_pack writing into [L, H, D] views (e.g. slices of persistent Q / KV buffers)."""
-    _ops.qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out)
+def qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, q_out, k_out, v_out, eps=1e-6,
+                            k_pre_out=None):
+    """qkv_norm_rope_pack writing into [L, H, D] views (e.g. slices of persistent Q / KV buffers);
+    k_pre_out (same strides), if given, receives the normalised k before rotation."""
+    _ops.qkv_norm_rope_pack_into(qkv, num_heads, q_weight, k_weight, cos, sin, eps, q_out, k_out, v_out, k_pre_out)
+
+
+def cached_k_rotate_into(key, cos, sin, out_key):
+    """RoPE of pre-RoPE cached keys [L, H, 128] into out_key [L, H, 128] (contiguous) with fp32
+    full-width cos/sin [L, 128]: the keys of fused_cached_kv_pack, without the value copy."""
+    _ops.cached_k_rotate_into(key, cos, sin, out_key)
 
 
 def qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, q_host, k_host, v_host, eps=1e-6,
@@ -272,6 +294,12 @@ def qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, q
     packs and downloads overlap chunk by chunk (chunk_tokens tokens each)."""
     _ops.qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, eps, head_major, q_host, k_host,
                                  v_host, chunk_tokens)
+
+
+def attn_merge(o_a, lse_a, o_b, lse_b):
+    """Attention over the union of two disjoint key sets from the two partial results:
+    o_a / o_b [1, H, S, D] with their log-sum-exps lse_a / lse_b fp32 [1, H, S] -> [S, H, D]."""
+    return _ops.attn_merge(o_a, lse_a, o_b, lse_b)
 
 
 def gelu_quant_fp8(x):

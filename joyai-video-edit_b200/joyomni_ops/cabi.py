@@ -62,6 +62,7 @@ SIGNATURES = {
     "jo_timestep_mlp_noalloc": [P, P, I64, P, P, I64, I64, P, P, P, P, I64, F32, P],
     "jo_timestep_mlp_modulate": [P, P, P, I64, P, I64, P, P, I64, I64, P, P, P, P, I64, P, I64, F32, P],
     "jo_qkv_norm_rope_pack_host": [P, P, P, I64, I64, P, P, P, P, P, I64, I64, I64, P, P, P, P, F32, I64, P, P, P],
+    "jo_attn_merge": [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, I64, I64, I64, I32, P],
     "jo_rmsnorm_quant_fp8": [P, I64, P, P, I64, P, I64, I64, I32, F32, P],
     "jo_norm_scale_shift_quant_fp8": [P, I64, P, P, I64, P, P, P, P, I64, I64, I64, I64, I32, I32, F32, P],
     "jo_gelu_quant_fp8": [P, I64, P, P, I64, I64, I64, I32, P],

@@ -8,18 +8,27 @@ fused sm_100a ops of this package:
              QKV FP8 GEMM (+bias)                fp8_scaled_mm                   (dit.py:408, fp8_linear.py:114-141)
              q/k RMSNorm + 3D RoPE + pack        qkv_norm_rope_pack_into         (dit.py:409-429, 489-496)
                (text rows: RMSNorm only)           -> persistent Q / KV buffers (no concatenation copy)
-    joint attention over [cache | img | txt]     torch SDPA (library, as FA4 in the reference, dit.py:498)
+    joint attention over [cache | img | txt]     cuDNN attention (library, as FA4 in the reference, dit.py:498);
+                                                 split at the cache rows + attn_merge when sequence parallel
     img/txt: attn quant + out-proj GEMM          sgl_per_token_quant_fp8, fp8_scaled_mm
              gated residual + LN2 + mod + quant  gated_residual_norm_scale_shift_quant_fp8 (dit.py:525-535)
              MLP up GEMM, GELU-tanh + quant      fp8_scaled_mm, gelu_quant_fp8   (dit.py:508-513)
              MLP down GEMM + gated residual      fp8_scaled_mm_gated_residual    (dit.py:536-538)
 
-Sequence parallel: the video tokens of the chunk are sharded over the ranks of
-``group``; each rank writes its K/V rows into its slice of the persistent KV
-buffer and an in-place NCCL ``all_gather_into_tensor`` (on a side stream,
-overlapped with the text stream) completes the current chunk's K/V before
-attention.  The text stream (512 tokens) is replicated.  The prior-chunk cache
-rows of the KV buffer are assumed replicated (gathered once when stored).
+Sequence parallel: the video and the text tokens of the chunk are both sharded
+over the ranks of ``group`` (every op but attention is per token); each rank
+writes its K/V rows, [its video | its text], as one block of the persistent KV
+buffer and one in-place NCCL ``all_gather_into_tensor`` per tensor (on a side
+stream) completes the chunk's K/V.  The gather overlaps the attention over the
+cache rows, which every rank holds already: attention is split into the cache
+rows and the gathered rows, and the two partial results are merged by their
+log-sum-exps (``attn_merge``).  The cache rows are replicated when a chunk is
+stored (``store_chunk_kv``: one gather of the stored chunk's pre-RoPE K and V)
+and rotated into the buffer once per window (``rotate_cache``).
+
+The modulation rows of every block come from one launch of the timestep MLP
+(``timestep_mlp_modulate``: the ModulateWan add of dit.py:103-116 folded into
+time_proj), or are formed here from the block's tables and ``vec``.
 """
 from __future__ import annotations
 
@@ -115,52 +124,126 @@ def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
 class KVBuffers:
     """Persistent joint-attention buffers (token-major [tokens, heads, head_dim]).
 
-    KV rows: [ cache (prior chunks, replicated) | current chunk video tokens (all ranks) | text ].
-    Q rows:  [ this rank's video tokens | text ].
+    KV rows: [ cache (prior chunks, replicated) | rank 0's block | rank 1's block | ... ],
+             a rank's block = [ its video tokens of the chunk | its text tokens ].
+    Q rows:  [ this rank's video tokens | this rank's text tokens ].
+
+    Both token streams are sharded over the ranks and every rank's K/V rows are one
+    contiguous block, so a single in-place all-gather completes the keys; the order of
+    the keys does not matter to (non-causal) attention.  With one rank the rows are
+    [ cache | video | text ].
+
+    The cache rows are ``slots`` chunk-sized slots (attention does not depend on the
+    order of its keys, so a new chunk takes the slot of the one it evicts).  For the
+    store path the buffers also keep every cached chunk's pre-RoPE keys (``k_pre``,
+    one more slot than the window: the chunk being stored goes to the spare one while
+    the window still attends over the chunk it will evict) and a staging block for
+    the stored chunk's values (``v_stage``); ``k_pre_of[i]`` is the ``k_pre`` slot of
+    cache slot i.
     """
 
     def __init__(self, cache_len: int, img_len: int, txt_len: int, heads: int, head_dim: int, world: int,
-                 device, dtype=BF16):
+                 device, dtype=BF16, store: bool = False):
         self.cache_len, self.img_len, self.txt_len = cache_len, img_len, txt_len
+        if img_len % world or txt_len % world:
+            raise ValueError(f"{img_len} video / {txt_len} text tokens do not split evenly over {world} ranks")
         self.local = img_len // world
+        self.txt_local = txt_len // world
+        self.block = self.local + self.txt_local
         s_kv = cache_len + img_len + txt_len
         self.k = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
         self.v = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
-        self.q = torch.empty(self.local + txt_len, heads, head_dim, dtype=dtype, device=device)
+        self.q = torch.empty(self.block, heads, head_dim, dtype=dtype, device=device)
+        self.slots = cache_len // img_len
+        self.k_pre = self.v_stage = None
+        if store:
+            if cache_len % img_len:
+                raise ValueError(f"a storing cache ({cache_len} rows) must hold whole chunks of {img_len} rows")
+            self.k_pre = torch.empty(self.slots + 1, img_len, heads, head_dim, dtype=dtype, device=device)
+            self.v_stage = torch.empty(img_len, heads, head_dim, dtype=dtype, device=device)
+        self.k_pre_of = list(range(self.slots))
+        self.spare = self.slots
+
+    def cache_slot_rows(self, slot: int):
+        return slice(slot * self.img_len, (slot + 1) * self.img_len)
+
+    def block_rows(self, rank: int):
+        b = self.cache_len + rank * self.block
+        return slice(b, b + self.block)
 
     def img_kv_rows(self, rank: int):
-        b = self.cache_len + rank * self.local
+        b = self.cache_len + rank * self.block
         return slice(b, b + self.local)
 
-    def chunk_kv_rows(self):
-        return slice(self.cache_len, self.cache_len + self.img_len)
+    def txt_kv_rows(self, rank: int):
+        b = self.cache_len + rank * self.block + self.local
+        return slice(b, b + self.txt_local)
 
-    def txt_kv_rows(self):
-        e = self.cache_len + self.img_len
-        return slice(e, e + self.txt_len)
+    def gathered_rows(self):
+        """Every rank's block (all rows after the cache)."""
+        return slice(self.cache_len, self.cache_len + self.img_len + self.txt_len)
+
+
+def store_chunk_kv(bufs: KVBuffers, rank: int, group) -> None:
+    """After a store forward (``block_forward(..., store=True)``): the chunk's pre-RoPE keys
+    (in the spare ``k_pre`` slot, each rank's own rows) and values (each rank's chunk rows
+    of ``v``) are gathered once, so every rank holds the whole stored chunk
+    (dit.py:445-459: the K/V handed to the cache writer; pre-RoPE keys, dit.py:413-429)."""
+    k_spare = bufs.k_pre[bufs.spare]
+    mine = slice(rank * bufs.local, (rank + 1) * bufs.local)
+    if group is None:
+        bufs.v_stage.copy_(bufs.v[bufs.img_kv_rows(rank)])
+        return
+    import torch.distributed as dist
+
+    dist.all_gather_into_tensor(k_spare, k_spare[mine], group=group)
+    dist.all_gather_into_tensor(bufs.v_stage, bufs.v[bufs.img_kv_rows(rank)], group=group)
+
+
+def advance_window(bufs: KVBuffers, evict_slot: int) -> None:
+    """The stored chunk replaces cache slot ``evict_slot``: its values move into the slot's
+    rows of ``v``, its pre-RoPE keys' slot is swapped in (the evicted chunk's becomes the
+    spare).  Call ``rotate_cache`` afterwards: the window's temporal positions changed."""
+    bufs.v[bufs.cache_slot_rows(evict_slot)].copy_(bufs.v_stage)
+    bufs.k_pre_of[evict_slot], bufs.spare = bufs.spare, bufs.k_pre_of[evict_slot]
+
+
+def rotate_cache(bufs: KVBuffers, cos: torch.Tensor, sin: torch.Tensor) -> None:
+    """RoPE of every cached chunk's pre-RoPE keys into the cache rows of ``k`` with the
+    window-relative fp32 full-width tables cos/sin [cache_len, head_dim] (row r for cache
+    row r): the key half of fused_cached_kv_pack (fused_joint_qkv_pack.cu:166-220;
+    dit.py:216-271), done once per window instead of once per block call."""
+    for i in range(bufs.slots):
+        rows = bufs.cache_slot_rows(i)
+        jo.cached_k_rotate_into(bufs.k_pre[bufs.k_pre_of[i]], cos[rows], sin[rows], bufs.k[rows])
 
 
 def gather_chunk_kv(bufs: KVBuffers, rank: int, group) -> None:
     """In-place all-gather of the current chunk's K/V rows over ``group``: every rank
-    contributes its own slice, every rank ends with all video tokens of the chunk."""
+    contributes its block (its video and text tokens), every rank ends with all of them."""
     import torch.distributed as dist
 
     for t in (bufs.k, bufs.v):
-        full = t[bufs.chunk_kv_rows()]
-        dist.all_gather_into_tensor(full, t[bufs.img_kv_rows(rank)], group=group)
+        dist.all_gather_into_tensor(t[bufs.gathered_rows()], t[bufs.block_rows(rank)], group=group)
 
 
 def modulation(table: torch.Tensor, vec: torch.Tensor):
     """ModulateWan (dit.py:103-116): table [6, D] + vec [6, D] -> six [1, D] rows."""
-    m = (table + vec).contiguous()
+    return mod_rows((table + vec).contiguous())
+
+
+def mod_rows(m: torch.Tensor):
+    """Six [1, D] modulation rows (shift1, scale1, gate1, shift2, scale2, gate2) of m [6, D]
+    (or [6 * D]), e.g. one block's rows of timestep_mlp_modulate's output."""
+    m = m.reshape(NUM_MOD, -1)
     return [m[i:i + 1] for i in range(NUM_MOD)]
 
 
-def _stream_qkv(x, w: StreamWeights, m, heads, cos, sin, q_out, k_out, v_out, trace=None, tag=""):
+def _stream_qkv(x, w: StreamWeights, m, heads, cos, sin, q_out, k_out, v_out, trace=None, tag="", k_pre_out=None):
     shift1, scale1 = m[0], m[1]
     xq, xs = jo.norm_scale_shift_quant_fp8(x, None, None, scale1, shift1, "layer", 1e-6)
     qkv = w.qkv(xq, xs)
-    jo.qkv_norm_rope_pack_into(qkv, heads, w.q_norm, w.k_norm, cos, sin, q_out, k_out, v_out, 1e-6)
+    jo.qkv_norm_rope_pack_into(qkv, heads, w.q_norm, w.k_norm, cos, sin, q_out, k_out, v_out, 1e-6, k_pre_out)
     if trace is not None:
         trace.update({f"{tag}.xq": xq, f"{tag}.xs": xs, f"{tag}.qkv": qkv})
 
@@ -189,6 +272,29 @@ def _event(stream) -> torch.cuda.Event:
     return e
 
 
+def attention_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    """Non-causal attention of token-major [S, H, D] buffers with its log-sum-exp: the
+    library (cuDNN) kernel, as SDPA picks it for these shapes.  Returns (o [1, H, Sq, D],
+    lse fp32 [1, H, Sq])."""
+    qh, kh, vh = (t.unsqueeze(0).transpose(1, 2) for t in (q, k, v))
+    r = torch.ops.aten._scaled_dot_product_cudnn_attention(qh, kh, vh, None, True, 0.0, False, False)
+    lse = r[1]
+    if lse.dim() == 4:  # [1, H, Sq, 1] on some library versions
+        lse = lse.squeeze(-1)
+    return r[0], lse
+
+
+def attention_split(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, split: int, before_rest=None):
+    """Attention of q over all rows of k/v as two parts merged by log-sum-exp: rows [0, split)
+    first, then ``before_rest()`` (e.g. a wait for the rest of the rows), then rows [split, S).
+    Returns [Sq, H*D] like ``attention``."""
+    oa, la = attention_lse(q, k[:split], v[:split])
+    if before_rest is not None:
+        before_rest()
+    ob, lb = attention_lse(q, k[split:], v[split:])
+    return jo.attn_merge(oa, la, ob, lb).reshape(q.shape[0], -1)
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     """Non-causal joint attention on token-major [S, H, D] buffers -> [Sq, H*D]."""
     out = F.scaled_dot_product_attention(q.unsqueeze(0).transpose(1, 2), k.unsqueeze(0).transpose(1, 2),
@@ -199,28 +305,41 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor
 def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                   w: BlockWeights, bufs: KVBuffers, group=None, rank: int = 0,
                   side_stream: Optional[torch.cuda.Stream] = None, trace: Optional[dict] = None,
-                  events: Optional[dict] = None):
+                  events: Optional[dict] = None, mods: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                  store: bool = False):
     """One double-stream block for one chunk.
 
-    img: bf16 [L_local, D] (this rank's video tokens), txt: bf16 [L_txt, D],
-    vec: bf16 [6, D] (time_proj output, dit.py:1165-1166), cos/sin: bf16 [L_local, head_dim/2]
-    for this rank's video tokens.  The cache rows of ``bufs.k/v`` hold the prior chunks.
-    Returns (img_out [L_local, D], txt_out [L_txt, D]).  ``trace`` (a dict), if
+    img: bf16 [L_local, D] (this rank's video tokens), txt: bf16 [T_local, D] (this rank's
+    text tokens), vec: bf16 [6, D] (time_proj output, dit.py:1165-1166), cos/sin: bf16
+    [L_local, head_dim/2] for this rank's video tokens.  The cache rows of ``bufs.k/v``
+    hold the prior chunks.  Returns (img_out [L_local, D], txt_out [T_local, D]).  ``trace`` (a dict), if
     given, receives every intermediate tensor (for stage-by-stage parity tests).
     ``events`` (a dict), if given with a group, receives timing CUDA events:
     "gather_start" / "gather_end" around the K/V all-gather on the side stream and
     "overlap_end" on the compute stream once the work that overlaps it is queued,
     so the gather's exposed time is max(0, overlap_end -> gather_end).
+    ``mods`` (img rows, txt rows), each [6, D], replaces the ModulateWan add of ``vec``
+    and the block's tables (rows of ``timestep_mlp_modulate``'s output).
+    ``store``: a store forward (buffers made with ``store=True``): the image pack also
+    writes this rank's pre-RoPE keys into the spare ``k_pre`` slot; ``store_chunk_kv``
+    then replicates the chunk.
     """
     H = w.heads
     L = img.shape[0]
-    mi = modulation(w.img.mod_table, vec)
-    mt = modulation(w.txt.mod_table, vec)
+    if mods is not None:
+        mi, mt = mod_rows(mods[0]), mod_rows(mods[1])
+    else:
+        mi = modulation(w.img.mod_table, vec)
+        mt = modulation(w.txt.mod_table, vec)
+    k_pre = bufs.k_pre[bufs.spare][rank * bufs.local:(rank + 1) * bufs.local] if store else None
     _stream_qkv(img, w.img, mi, H, cos, sin, bufs.q[:L], bufs.k[bufs.img_kv_rows(rank)],
-                bufs.v[bufs.img_kv_rows(rank)], trace, "img")
+                bufs.v[bufs.img_kv_rows(rank)], trace, "img", k_pre)
+    _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows(rank)],
+                bufs.v[bufs.txt_kv_rows(rank)], trace, "txt")
     gathered = None
     if group is not None:
-        # complete the chunk's K/V on a side stream while the text stream runs
+        # complete the chunk's K/V (every rank's block) on a side stream; the attention
+        # over the cache rows runs meanwhile
         side = side_stream or torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -230,13 +349,19 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
             if events is not None:
                 events["gather_end"] = _event(side)
         gathered = side
-    _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows()], bufs.v[bufs.txt_kv_rows()],
-                trace, "txt")
-    if gathered is not None:
+
+    def join_gather():
         if events is not None:
             events["overlap_end"] = _event(torch.cuda.current_stream())
         torch.cuda.current_stream().wait_stream(gathered)
-    attn = attention(bufs.q, bufs.k, bufs.v)
+
+    if gathered is not None and bufs.cache_len > 0:
+        # the cache rows are here already: attend over them while the chunk's K/V arrive
+        attn = attention_split(bufs.q, bufs.k, bufs.v, bufs.cache_len, join_gather)
+    else:
+        if gathered is not None:
+            join_gather()
+        attn = attention(bufs.q, bufs.k, bufs.v)
     if trace is not None:
         trace.update({"q": bufs.q, "k": bufs.k, "v": bufs.v, "mi": mi, "mt": mt})
     img_out = _stream_out(img, attn[:L], w.img, mi, trace, "img")

@@ -169,3 +169,71 @@ def test_block_chain(dev, hidden, heads, ffn, img_len, txt_len, cache_len):
     # --- end to end against the oracle chain
     r_img, r_txt = ops.block_forward(img, txt, vec, cos, sin, W, ck, cv, heads)
     assert rel_err(img_out, r_img) < 2e-2 and rel_err(txt_out, r_txt) < 2e-2
+
+
+# ------------------------------------------------------------------ attention split + merge
+@pytest.mark.parametrize("Sq,S,split,H", [(300, 1000, 700, 4), (129, 257, 1, 2), (64, 4096, 3072, 24)])
+def test_attention_split_merge(jo, dev, Sq, S, split, H):
+    """Attention over [0, split) and [split, S) merged by log-sum-exp equals attention over
+    all rows: against the fp32 oracle within the tolerance of the single-call attention, and
+    the merge kernel against its own formula on the same partial results."""
+    from joyomni_ops import chain
+
+    q, k, v = rand((Sq, H, 128), 30).to(dev), rand((S, H, 128), 31).to(dev), rand((S, H, 128), 32).to(dev)
+    merged = chain.attention_split(q, k, v, split)
+    full = chain.attention(q, k, v)
+    ref = ops.attention(q.cpu(), k.cpu(), v.cpu())
+    err_full, err_split = rel_err(full, ref), rel_err(merged, ref)
+    assert err_split < 1e-2 and err_split <= 2 * err_full + 1e-3, (err_split, err_full)
+    # the merge kernel on the same partial results, against the formula in fp32 (the
+    # log-sum-exps are natural logarithms of the scaled scores)
+    oa, la = chain.attention_lse(q, k[:split], v[:split])
+    ob, lb = chain.attention_lse(q, k[split:], v[split:])
+    got = jo.attn_merge(oa, la, ob, lb)
+    m = torch.maximum(la, lb)
+    wa, wb = torch.exp(la - m), torch.exp(lb - m)
+    want = ((wa / (wa + wb))[..., None] * oa.float() + (wb / (wa + wb))[..., None] * ob.float())
+    want = want[0].transpose(0, 1).to(BF)  # [Sq, H, D]
+    assert_ulp_close(got, want, 1.0, what="attn_merge")
+    # the log-sum-exp convention: natural log of sum(exp(q.k / sqrt(D)))
+    s = (q[:4].float().transpose(0, 1) @ k[:split].float().permute(1, 2, 0)) / 128 ** 0.5
+    assert torch.allclose(la[0, :, :4].float(), torch.logsumexp(s, dim=-1), rtol=1e-3, atol=1e-2)
+
+
+# ------------------------------------------------------------------ KV store path
+def test_store_advance_rotate(dev):
+    """A store forward writes the chunk's pre-RoPE keys into the spare slot and its values
+    into the staging block; advancing the window moves them into the evicted slot; the
+    rotation of the cache equals the reference's cached K/V pack on the pre-RoPE keys."""
+    from joyomni_ops import chain, rope
+
+    hidden, heads, ffn, L, T = 256, 2, 512, 64, 16
+    w = chain.random_block_weights(hidden, heads, ffn, device=dev, seed=4)
+    bufs = chain.KVBuffers(2 * L, L, T, heads, 128, 1, dev, store=True)
+    for i in range(2):  # a window of two cached chunks with known pre-RoPE keys and values
+        bufs.k_pre[i].copy_(rand((L, heads, 128), 40 + i))
+        bufs.v[bufs.cache_slot_rows(i)].copy_(rand((L, heads, 128), 50 + i))
+    pre_before = bufs.k_pre.clone()
+    img, txt, vec = rand((L, hidden), 60).to(dev), rand((T, hidden), 61).to(dev), rand((6, hidden), 62, 0.1).to(dev)
+    cos, sin = rope.video_chunk_tables(1, 8, L // 8, 5)
+    tr = {}
+    chain.block_forward(img, txt, vec, cos.to(dev), sin.to(dev), w, bufs, trace=tr, store=True)
+    chain.store_chunk_kv(bufs, 0, None)
+    torch.cuda.synchronize()
+    W = CpuBlock(w)
+    _, _, rv, rpre = ops.qkv_norm_rope_pack(tr["img.qkv"].cpu(), heads, W.img.q_norm, W.img.k_norm, cos, sin, 1e-6,
+                                            head_major=False, with_pre=True)
+    assert_ulp_close(bufs.k_pre[bufs.spare], rpre, 1.0, what="stored pre-RoPE keys")
+    assert torch.equal(bufs.v_stage.cpu(), rv)
+    assert torch.equal(bufs.k_pre[:2], pre_before[:2]), "the window's own slots must not change"
+    spare = bufs.spare
+    chain.advance_window(bufs, 1)  # the stored chunk replaces cache slot 1
+    assert bufs.k_pre_of == [0, spare] and bufs.spare == 1
+    assert torch.equal(bufs.v[bufs.cache_slot_rows(1)].cpu(), rv)
+    # window-relative tables for the two slots: full-width fp32 [2L, 128]
+    (cf, sf), _ = ops.rope_video_tables(2, 8, L // 8, 3)
+    chain.rotate_cache(bufs, cf.to(dev), sf.to(dev))
+    torch.cuda.synchronize()
+    want_k, _ = ops.cached_kv_pack(bufs.k_pre[0].cpu()[None], bufs.v[:L].cpu()[None],
+                                   bufs.k_pre[spare].cpu()[None], bufs.v[L:2 * L].cpu()[None], cf, sf)
+    assert_ulp_close(bufs.k[:2 * L], want_k[0], 1.0, what="rotated cache keys")

@@ -1,7 +1,8 @@
 """Host logic of the sequence-parallel chain on CPU ranks (gloo, world_size 2).
 
-Checks the token sharding and the in-place K/V all-gather placement of
-joyomni_ops.chain (which on GPUs runs over NCCL), plus the failure path: a rank
+Checks the token sharding (video and text tokens) and the in-place K/V
+all-gather placement of joyomni_ops.chain (which on GPUs runs over NCCL): every
+rank's block [its video | its text] lands in its place, plus the failure path: a rank
 that never joins the collective makes the others fail with an error instead of
 hanging (short process-group timeout).
 """
@@ -34,16 +35,21 @@ def _worker(rank, world, port, mode, q):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
         from joyomni_ops import chain
 
-        cache, img, txt, H, D = 6, 8, 3, 2, 4
+        cache, img, txt, H, D = 6, 8, 4, 2, 4
         b0, b1 = chain.shard_range(img, world, rank)
         assert (b1 - b0) * world == img
         bufs = chain.KVBuffers(cache, img, txt, H, D, world, "cpu", dtype=torch.float32)
         bufs.k.fill_(-1.0)
         bufs.v.fill_(-2.0)
-        # each rank writes its own token rows: value = global token index (+0.5 for v)
-        tok = torch.arange(b0, b1, dtype=torch.float32).view(-1, 1, 1).expand(-1, H, D)
-        bufs.k[bufs.img_kv_rows(rank)] = tok
-        bufs.v[bufs.img_kv_rows(rank)] = tok + 0.5
+        # each rank writes its own token rows: value = global token index (+0.5 for v),
+        # text tokens 100 + index
+        def toks(a, b, base=0.0):
+            return (base + torch.arange(a, b, dtype=torch.float32)).view(-1, 1, 1).expand(-1, H, D)
+        t0, t1 = chain.shard_range(txt, world, rank)
+        bufs.k[bufs.img_kv_rows(rank)] = toks(b0, b1)
+        bufs.v[bufs.img_kv_rows(rank)] = toks(b0, b1) + 0.5
+        bufs.k[bufs.txt_kv_rows(rank)] = toks(t0, t1, 100.0)
+        bufs.v[bufs.txt_kv_rows(rank)] = toks(t0, t1, 100.0) + 0.5
         if mode == "absent" and rank == 1:
             q.put((rank, "skipped"))
             return  # never joins the collective
@@ -53,10 +59,17 @@ def _worker(rank, world, port, mode, q):
             # a rank whose buffers were sized for a different chunk length
             bufs = chain.KVBuffers(cache, img + 2 * world, txt, H, D, world, "cpu", dtype=torch.float32)
         chain.gather_chunk_kv(bufs, rank, None)
-        full = torch.arange(img, dtype=torch.float32).view(-1, 1, 1).expand(-1, H, D)
-        assert torch.equal(bufs.k[bufs.chunk_kv_rows()], full)
-        assert torch.equal(bufs.v[bufs.chunk_kv_rows()], full + 0.5)
-        assert (bufs.k[:cache] == -1).all() and (bufs.k[bufs.txt_kv_rows()] == -1).all()
+        for r in range(world):  # every rank's block, in rank order
+            rb0, rb1 = chain.shard_range(img, world, r)
+            rt0, rt1 = chain.shard_range(txt, world, r)
+            assert torch.equal(bufs.k[bufs.img_kv_rows(r)], toks(rb0, rb1))
+            assert torch.equal(bufs.v[bufs.img_kv_rows(r)], toks(rb0, rb1) + 0.5)
+            assert torch.equal(bufs.k[bufs.txt_kv_rows(r)], toks(rt0, rt1, 100.0))
+            assert torch.equal(bufs.v[bufs.txt_kv_rows(r)], toks(rt0, rt1, 100.0) + 0.5)
+        assert (bufs.k[:cache] == -1).all() and (bufs.v[:cache] == -2).all()
+        # the gathered rows are exactly every video and text token once
+        keys = sorted(bufs.k[bufs.gathered_rows(), 0, 0].tolist())
+        assert keys == sorted(list(range(img)) + [100.0 + i for i in range(txt)])
         q.put((rank, "ok"))
         dist.destroy_process_group()
     except Exception as e:  # reported to the parent

@@ -1,8 +1,9 @@
 """Sequence-parallel chain on 2 GPUs (NCCL) against the same chain on 1 GPU.
 
-Each rank computes its shard of the video tokens; the shards, concatenated,
-must equal the single-GPU block output (same kernels, same weights; attention
-sees the same full K/V, only the query batch differs).  Skipped with fewer
+Each rank computes its shard of the video and of the text tokens; the shards,
+concatenated, must equal the single-GPU block output (same kernels, same weights;
+attention sees the same keys, gathered in another order and split at the cache
+rows, merged by log-sum-exp).  Skipped with fewer
 than two visible GPUs.  Run with NCCL_NVLS_ENABLE=0 semantics not needed: no
 rank dies mid-collective here.
 """
@@ -46,10 +47,11 @@ def _run_chain(dev, world, rank, group):
 
     w, img, txt, vec, ck, cv, cos, sin = _inputs(dev)
     b0, b1 = chain.shard_range(IMG, world, rank)
+    t0, t1 = chain.shard_range(TXT, world, rank)
     bufs = chain.KVBuffers(CACHE, IMG, TXT, HEADS, 128, world, dev)
     bufs.k[:CACHE].copy_(ck)
     bufs.v[:CACHE].copy_(cv)
-    a, b = chain.block_forward(img[b0:b1].to(dev), txt.to(dev), vec.to(dev), cos[b0:b1].to(dev),
+    a, b = chain.block_forward(img[b0:b1].to(dev), txt[t0:t1].to(dev), vec.to(dev), cos[b0:b1].to(dev),
                                sin[b0:b1].to(dev), w, bufs, group=group, rank=rank)
     torch.cuda.synchronize()
     return a.cpu(), b.cpu()
@@ -94,7 +96,8 @@ def test_sp2_matches_single_gpu():
     for r in range(2):
         assert res[r][2] is None, res[r][2]
     img_sp = torch.cat([res[0][0], res[1][0]])
-    for got, want in ((img_sp, ref_img), (res[0][1], ref_txt), (res[1][1], ref_txt)):
+    txt_sp = torch.cat([res[0][1], res[1][1]])
+    for got, want in ((img_sp, ref_img), (txt_sp, ref_txt)):
         d = (got.float() - want.float()).abs().max().item()
         scale = want.float().abs().max().item()
         assert d <= 1e-2 * scale, f"SP result differs from single GPU by {d} (max |ref| {scale})"
