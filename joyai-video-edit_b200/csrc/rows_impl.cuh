@@ -27,7 +27,8 @@ namespace jo {
 namespace rows {
 
 // L2 hints of the staged path: 1 = row loads evict-first (each byte is read
-// once), 2 = the output stores too.
+// once), 2 = the output stores too.  Measured: +1.5 % on LN + modulate, -2 to -4 %
+// on the quant and the short RMSNorm, so off.
 #ifndef JO_ROW_HINT
 #define JO_ROW_HINT 0
 #endif
@@ -561,13 +562,17 @@ constexpr int kMaxWarps = 32;
 #endif
 constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
 // Groups with at most three rows in all keep every one of them in flight from
-// the start (1), or refill one slot at a time like longer matrices (0).
+// the start (1), or refill one slot at a time like longer matrices (0).  Measured
+// on RMSNorm [3600, 3072] (1-2 rows per group): 10.2 us with 1, 9.6 us with 0 --
+// loads issued as slots free up interleave the reads with the writes.
 #ifndef JO_ROW_SMALL_ALL
-#define JO_ROW_SMALL_ALL 1
+#define JO_ROW_SMALL_ALL 0
 #endif
 // Rows of more than 128 vectors split over two warps (half the vectors per
 // thread, twice the warps per SM) for: 0 = residual rows only, 1 = also rows
-// with a quantising epilogue, 2 = also every normalising op.
+// with a quantising epilogue, 2 = also every normalising op.  Measured at
+// [10800, 3072]: RMSNorm -> FP8 22.5 us with 0, 26.5 us with 1 or 2 (the
+// cross-warp reductions cost more than the extra warps hide).
 #ifndef JO_ROW_G2
 #define JO_ROW_G2 0
 #endif

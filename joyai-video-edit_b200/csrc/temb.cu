@@ -34,6 +34,13 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxK = 4096;                 // input features per layer
 constexpr int kMaxB = 8;                    // batch rows per launch
 constexpr uint32_t kBudget = 216u * 1024u;  // shared memory: batch rows + weight slots
+// Shared memory a layer aims to stay within: half an SM, so that the next layer's
+// CTAs (launched early, programmatic dependent launch) fit beside this layer's on
+// every SM and stream their first weight rows while this layer still runs.
+#ifndef JO_TEMB_LAYER_SMEM
+#define JO_TEMB_LAYER_SMEM (110u * 1024u)
+#endif
+constexpr uint32_t kLayerSmem = JO_TEMB_LAYER_SMEM;
 
 struct TembLayer {
   const __nv_bfloat16* x;  // [B, K] input rows (null for the sinusoid layer)
@@ -215,8 +222,10 @@ int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
     cfg.slot_bytes = ((uint32_t)cfg.rows_per_unit * row_bytes + 127u) & ~127u;
     cfg.x_off = 1024;  // after the warps' mbarriers
     cfg.data_off = (cfg.x_off + (uint32_t)kb * row_bytes + 127u) & ~127u;
-    const uint32_t avail = kBudget - cfg.data_off;
-    cfg.m = (int)std::min<uint32_t>(3u, avail / (kWarps * cfg.slot_bytes));
+    const uint32_t half = kLayerSmem > cfg.data_off ? kLayerSmem - cfg.data_off : 0u;
+    cfg.m = (int)std::min<uint32_t>(3u, half / (kWarps * cfg.slot_bytes));
+    if (cfg.m < 1)  // rows too wide for half an SM: the whole budget, one CTA per SM
+      cfg.m = (int)std::min<uint32_t>(3u, (kBudget - cfg.data_off) / (kWarps * cfg.slot_bytes));
     if (cfg.m < 1) return fail(JO_ERR_SHAPE, "timestep_mlp: rows too large to stage");
     const size_t smem = cfg.data_off + (size_t)kWarps * cfg.m * cfg.slot_bytes;
     // CTAs: one per SM (fewer only when there are fewer units than SMs)

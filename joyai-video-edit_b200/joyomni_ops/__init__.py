@@ -288,7 +288,7 @@ def cached_k_rotate_into(key, cos, sin, out_key):
 
 
 def qkv_norm_rope_pack_host(qkv_host, num_heads, q_weight, k_weight, cos, sin, q_host, k_host, v_host, eps=1e-6,
-                            head_major=True, chunk_tokens=1350):
+                            head_major=True, chunk_tokens=675):
     """qkv_norm_rope_pack from a pinned host qkv [L, 3*H*D] into pinned host q/k/v
     ([H, L, D] head-major, else [L, H, D]); weights and cos/sin on the GPU.  Uploads,
     packs and downloads overlap chunk by chunk (chunk_tokens tokens each)."""
