@@ -9,7 +9,7 @@ pass of the op over one chunk.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload qkv_pack|rmsnorm|ln_mod|gated_ln|gelu|silu_mul|quant|rmsnorm_quant|
-                                gemm_qkv|gemm_up|temb|chain] [--no-per-op] [--no-chain]
+                                gelu_quant|gemm_qkv|gemm_up|temb|chain] [--no-per-op] [--no-chain]
 
 The default line also carries ``per_op`` (every other BASELINE config at 1 GPU,
 each with its roofline fraction and a short CPU baseline) and ``chain`` (the
@@ -176,7 +176,7 @@ class RowOp(Workload):
         self.shape = {"rows": M, "cols": N}
 
     def algo_bytes(self):
-        scales = self.M * 4 if self.name in ("quant", "rmsnorm_quant") else 0  # fp32 scale per token
+        scales = self.M * 4 if self.name in ("quant", "rmsnorm_quant", "gelu_quant") else 0  # fp32 scale per token
         return int(self.M * self.N * (self.reads + self.writes)) + scales
 
     def _inputs(self, seed, dev):
@@ -190,7 +190,7 @@ class RowOp(Workload):
             return dict(x=r(M, N), scale=r(1, N, sc=0.1), shift=r(1, N, sc=0.1))
         if n == "gated_ln":
             return dict(res=r(M, N), x=r(M, N), gate=r(1, N, sc=0.1), scale=r(1, N, sc=0.1), shift=r(1, N, sc=0.1))
-        if n == "gelu":
+        if n in ("gelu", "gelu_quant"):
             return dict(x=r(M, N))
         if n == "silu_mul":
             return dict(a=r(M, N), b=r(M, N))
@@ -228,6 +228,8 @@ class RowOp(Workload):
             return q, s
         if n == "rmsnorm_quant":
             return jo.rmsnorm_quant_fp8(x["x"], x["w"], 1e-6)
+        if n == "gelu_quant":
+            return jo.gelu_quant_fp8(x["x"])
         raise ValueError(n)
 
     def e2e_step(self, st, host_in, host_out):
@@ -260,6 +262,8 @@ class RowOp(Workload):
             return ops.per_token_quant_fp8(x["x"])
         if n == "rmsnorm_quant":
             return ops.rmsnorm_quant_fp8(x["x"], x["w"], 1e-6)
+        if n == "gelu_quant":
+            return ops.per_token_quant_fp8(ops.gelu_tanh(x["x"]))
         raise ValueError(n)
 
 
@@ -427,6 +431,41 @@ class Chain(Workload):
         host_out["img_out"].copy_(a, non_blocking=True)
         host_out["txt_out"].copy_(b, non_blocking=True)
 
+    CPU_FRACTION = 16  # the CPU sample: 1/16 of the video and text tokens
+
+    def make_cpu(self, seed):
+        """A bounded CPU sample of the block: the oracle chain (the reference's FP8 block,
+        dit.py:360-558, restated in oracle/ops.py) for 1/16 of the chunk's video and text
+        tokens, attending over the whole 4-chunk cache plus the sampled tokens."""
+        from types import SimpleNamespace as NS
+
+        from oracle import ops
+
+        g = torch.Generator().manual_seed(seed)
+        D, H, F = self.D, self.H, self.F
+
+        def lin(n, k):
+            wq, ws = ops.quantize_weight_per_channel((0.02 * torch.randn(n, k, generator=g)).to(BF))
+            return NS(wq=wq, ws=ws, bias=(0.02 * torch.randn(n, generator=g)).to(BF))
+
+        def stream():
+            return NS(mod_table=(torch.randn(6, D, generator=g) / D ** 0.5).to(BF),
+                      qkv=lin(3 * D, D), q_norm=(1 + 0.02 * torch.randn(128, generator=g)).to(BF),
+                      k_norm=(1 + 0.02 * torch.randn(128, generator=g)).to(BF), proj=lin(D, D), up=lin(F, D),
+                      down=lin(D, F))
+
+        L, T = self.L // self.CPU_FRACTION, self.T // self.CPU_FRACTION
+        (_, _), (cos, sin) = ops.rope_video_tables(3, 45, 80, 7)
+        return dict(w=NS(img=stream(), txt=stream()), img=torch.randn(L, D, generator=g).to(BF),
+                    txt=torch.randn(T, D, generator=g).to(BF), vec=(0.1 * torch.randn(6, D, generator=g)).to(BF),
+                    cos=cos[:L], sin=sin[:L], ck=torch.randn(self.CACHE, H, D // H, generator=g).to(BF),
+                    cv=torch.randn(self.CACHE, H, D // H, generator=g).to(BF))
+
+    def cpu_step(self, x):
+        from oracle import ops
+
+        return ops.block_forward(x["img"], x["txt"], x["vec"], x["cos"], x["sin"], x["w"], x["ck"], x["cv"], self.H)
+
 
 def measure_fp8_peak(dev, seconds=1.0):
     """cuBLASLt FP8 (torch._scaled_mm, 8192^3, row/col scales), back to back: TFLOP/s."""
@@ -463,6 +502,9 @@ def workloads():
         "silu_mul": RowOp("silu_mul", 10800, 8192, 4, 2, "SiLU-gated mul 2x[10800,8192] (configs[2])"),
         "quant": RowOp("quant", 10800, 3072, 2, 1, "per-token FP8 quant [10800,3072] (configs[3])"),
         "rmsnorm_quant": RowOp("rmsnorm_quant", 10800, 3072, 2, 1, "RMSNorm->FP8 quant [10800,3072] (configs[3])"),
+        "gelu_quant": RowOp("gelu_quant", 10800, 12288, 2, 1,
+                            "GELU-tanh -> FP8 quant [10800,12288] (the block's MLP activation + down-projection "
+                            "quant, configs[2]/[4])"),
         "gemm_qkv": Gemm("gemm_qkv", 10800, 9216, 3072, "FP8 GEMM QKV projection [10800,3072]x[3072,9216] (configs[3])"),
         "gemm_up": Gemm("gemm_up", 10800, 12288, 3072, "FP8 GEMM MLP-up [10800,3072]x[3072,12288] (configs[3])"),
         "chain": Chain(),
@@ -612,15 +654,16 @@ def time_allgather(wl, st, world: int, rank: int, iters: int = 10) -> dict:
     total = 2 * (wl.L + wl.T) * wl.D * 2  # K and V rows of the chunk (video + text), bf16
     return {"us": round(ms * 1e3, 1), "bytes_received_per_rank": int(total * (world - 1) / world),
             "bus_gbs": round(total * (world - 1) / world / (ms * 1e-3) / 1e9, 1),
-            "note": "in-place all_gather_into_tensor of the chunk's K and V (NCCL), alone; in the "
-                    "block it overlaps the text stream on a side stream"}
+            "note": "in-place all_gather_into_tensor of the chunk's K and V rows of every rank (NCCL), alone; "
+                    "in the block it runs on a side stream beside the attention over the cache rows"}
 
 
 def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
     """The reference's CPU path (oracle restatement of its PyTorch code) on the host cores."""
     torch.set_num_threads(os.cpu_count() or 1)
     x = wl.make_cpu(seed=1)
-    wl.cpu_step(x)  # warm-up
+    if not isinstance(wl, Chain):  # the block sample is seconds of large-matrix work: no warm-up pass
+        wl.cpu_step(x)
     n, t0 = 0, time.perf_counter()
     while True:
         wl.cpu_step(x)
@@ -629,6 +672,13 @@ def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
         if el >= min_seconds or n >= 200:
             break
     thr = torch.get_num_threads()
+    if isinstance(wl, Chain):
+        f = wl.CPU_FRACTION
+        return {"value": round(el / n * 1e6 * f, 1), "unit": "us", "cores": thr, "kind": "port",
+                "sample": f"{n} pass(es) of the oracle block (the reference's FP8 block restated, fp32 attention, "
+                          f"float64 GEMMs) for 1/{f} of the video and text tokens ({wl.L // f} + {wl.T // f}) "
+                          f"attending over the 4-chunk cache plus the sampled tokens, {el:.1f} s, extrapolated "
+                          f"x{f} to one block; {thr} threads"}
     if isinstance(wl, Gemm):
         return {"value": round(2 * x["rows"] * wl.N * wl.K * n / el / 1e12, 5), "unit": "TFLOP/s", "cores": thr,
                 "kind": "port", "sample": f"{n} x {x['rows']} rows of A against the full B, fp32 dequantised "
@@ -765,8 +815,8 @@ def run_headline(args, wl: Workload, world: int, rank: int, local: int, dev):
     }
 
 
-PER_OP = ["rmsnorm", "ln_mod", "gated_ln", "gelu", "silu_mul", "quant", "rmsnorm_quant", "gemm_qkv", "gemm_up",
-          "temb"]
+PER_OP = ["rmsnorm", "ln_mod", "gated_ln", "gelu", "silu_mul", "quant", "rmsnorm_quant", "gelu_quant", "gemm_qkv",
+          "gemm_up", "temb"]
 
 
 def run_per_op(args, dev, local: int) -> dict:
@@ -841,6 +891,8 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
                                 hidden_frac=round(max(0.0, 1 - ex * 1e3 / g_us), 3) if g_us > 0 else None)
     del st
     torch.cuda.empty_cache()
+    if world == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_baseline(wl, min_seconds=1.0)
     return rec
 
 

@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
 // output ulp); the regrouped products move the fp32 result by a few fp32 ulps
 // (at most one bf16 ulp after rounding).
 #ifndef JO_QK_WARPS
-#define JO_QK_WARPS 12
+#define JO_QK_WARPS 8
 #endif
 #ifndef JO_QK_SLOTS
 #define JO_QK_SLOTS 1
@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(kThreads) qk_norm_rope_kernel(const QkArgs a) 
 #ifndef JO_QK_HINT
 #define JO_QK_HINT 2
 #endif
-constexpr int kQkWarps = JO_QK_WARPS;  // config 1: 72.5 us with 16 warps, 71.9 with 12
+// config 1: 72.5 us with 16 warps, 71.6 with 12, 71.1 with 10, 69.5 with 8
+constexpr int kQkWarps = JO_QK_WARPS;
 constexpr int kQkSlots = JO_QK_SLOTS;  // 6 KB units in flight per warp (two, 15 warps: 4.5 % slower)
 // L2 hints: 1 = the unit loads are evict-first (each byte is read once), 2 = the
 // output stores too (measured at config 1: 74.7 us without, 73.4 with 1, 73.1 with 2)

@@ -576,8 +576,16 @@ constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
 #ifndef JO_ROW_G2
 #define JO_ROW_G2 0
 #endif
-// threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread)
-constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : 512); }
+// Upper bound on the warps of a staged CTA (0: as many as the register budget allows).
+#ifndef JO_ROW_WARPS_CAP
+#define JO_ROW_WARPS_CAP 0
+#endif
+// threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread);
+// JO_ROW_T12 sets it for 9-12 vectors per thread (3072-wide bf16 rows)
+#ifndef JO_ROW_T12
+#define JO_ROW_T12 512
+#endif
+constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : (vpt <= 12 ? JO_ROW_T12 : 512)); }
 
 struct StagedCfg {
   int warps;            // warps per CTA (blockDim.x / 32), a multiple of G
@@ -857,6 +865,8 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   if (cfg.G * 32 * kVPT < nvec) return fail(JO_ERR_SHAPE, "row kernel: row group too small");
   cfg.warps = staged_threads(kVPT) / 32;
   if (cfg.G == 2 && cfg.warps > 30) cfg.warps = 30;
+  if (JO_ROW_WARPS_CAP > 0 && cfg.warps > JO_ROW_WARPS_CAP)
+    cfg.warps = JO_ROW_WARPS_CAP >= cfg.G ? JO_ROW_WARPS_CAP / cfg.G * cfg.G : cfg.G;
   const uint32_t cache_bytes = (uint32_t)(Sets<kF>::n * 4 * a.cols + 127) & ~127u;
   if (cache_bytes + 2048u >= kBudget) return fail(JO_ERR_SHAPE, "row kernel: rows too large to stage");
   const uint32_t avail = kBudget - cache_bytes - 2048u;
@@ -950,13 +960,18 @@ int launch_rows_t(const RowArgs& a, cudaStream_t st) {
   if (int s = device_info(&di)) return s;
   if (row_vec_ok(a, sizeof(T))) {
     const int nvec = (int)(a.cols / V);
-    if (nvec <= 32 * 16 && staged_operands_ok(a, kPro)) {
+    // staged rows: up to 512 vectors (4096 bf16) per warp-owned row, residual rows up to
+    // 512 vectors in groups of up to 4 warps, and wider single-input rows (up to 2048
+    // vectors: the MLP activation's 12288 bf16) in groups of 2-4 warps
+    const int max_staged = kPro == kResidGate ? 32 * 16 : 4 * 32 * 16;
+    if (nvec <= max_staged && staged_operands_ok(a, kPro)) {
 #define JO_STAGED(VPT) return launch_staged<T, VPT, kNorm, kPro, kEpi>(a, st, di)
       // vectors per thread: one warp per row, or (residual + x rows) the
       // smallest row group G in {1, 2, 4} with at most 4 vectors per thread
       const bool split = kPro == kResidGate || (JO_ROW_G2 >= 1 && kEpi == kQuantY && kNorm != kNoNorm) ||
                          (JO_ROW_G2 >= 2 && kNorm != kNoNorm);
-      const int G = !split || nvec <= 128 ? 1 : (kPro != kResidGate || nvec <= 256 ? 2 : 4);
+      int G = !split || nvec <= 128 ? 1 : (kPro != kResidGate || nvec <= 256 ? 2 : 4);
+      if (kPro != kResidGate && nvec > 32 * 16) G = nvec <= 2 * 32 * 12 ? 2 : 4;  // <= 12 (16) vectors per thread
       const int vpt = (nvec + 32 * G - 1) / (32 * G);
       if (vpt <= 2) JO_STAGED(2);
       if (vpt <= 3) JO_STAGED(3);

@@ -34,11 +34,13 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxK = 4096;                 // input features per layer
 constexpr int kMaxB = 8;                    // batch rows per launch
 constexpr uint32_t kBudget = 216u * 1024u;  // shared memory: batch rows + weight slots
-// Shared memory a layer aims to stay within: half an SM, so that the next layer's
-// CTAs (launched early, programmatic dependent launch) fit beside this layer's on
-// every SM and stream their first weight rows while this layer still runs.
+// Shared memory a layer aims to stay within.  At half an SM (110 KB) the next
+// layer's CTAs, launched early (programmatic dependent launch), fit beside this
+// layer's and stream their first weight rows while it runs; measured at batch 1
+// that is slower than the whole budget (35.2 vs 33.6 us: the big last layer keeps
+// fewer rows in flight), so each layer takes the whole budget.
 #ifndef JO_TEMB_LAYER_SMEM
-#define JO_TEMB_LAYER_SMEM (110u * 1024u)
+#define JO_TEMB_LAYER_SMEM (216u * 1024u)
 #endif
 constexpr uint32_t kLayerSmem = JO_TEMB_LAYER_SMEM;
 
@@ -200,6 +202,125 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(bar0 + 8u * (uint32_t)(j % m), (uint32_t)((j / m) & 1), fault);
 }
 
+// Small layers (the first two at the model's shape: 1.5 MB and 19 MB of weights)
+// are bound by latency, not bandwidth: one warp per output row loads its whole
+// weight row into registers with direct 16-byte loads -- before the wait on the
+// previous layer when that layer is one of ours (kEarly), so the loads overlap it;
+// the CTAs use no dynamic shared memory and fit beside the previous layer's --
+// then the batch rows.  The per-lane summation order is the staged kernel's
+// (elements lane*8 + j*256, two fma chains per vector), so the bits are the same.
+constexpr int kDirectWarps = 8;
+constexpr int kDirectMaxB = 2;
+
+template <int kB, int kV, bool kSinIn, bool kSilu, bool kEarly>
+__global__ void __launch_bounds__(kDirectWarps * 32) temb_direct_kernel(const TembLayer a, int b0) {
+  __shared__ __align__(16) __nv_bfloat16 xs[kB * kV * 256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = a.K;
+  const int64_t n = (int64_t)blockIdx.x * kDirectWarps + warp;
+  const bool row_ok = n < a.N;
+  uint4 w[kV];
+  auto load_w = [&]() {
+#pragma unroll
+    for (int j = 0; j < kV; ++j) {
+      const int kk = lane * 8 + j * 256;
+      w[j] = (row_ok && kk < K) ? ld_stream(a.w + n * K + kk) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if constexpr (kEarly) load_w();
+  pdl_wait();  // the previous layer's output (our input) is complete from here on
+  pdl_trigger();
+  if constexpr (!kEarly) load_w();
+  if constexpr (kSinIn) {  // the sinusoid, with the staged kernel's arithmetic
+    const int half = K / 2;
+    for (int idx = threadIdx.x; idx < kB * half; idx += blockDim.x) {
+      const int b = idx / half, i = idx - b * half;
+      float c = 0.f, s = 0.f;
+      if (b0 + b < a.B) {
+        const float ex = __fdiv_rn(__fmul_rn(a.neg_log_period, (float)i), (float)half);
+        const float arg = __fmul_rn(a.t[b0 + b], expf(ex));
+        sincosf(arg, &s, &c);
+      }
+      xs[b * K + i] = __float2bfloat16_rn(c);
+      xs[b * K + half + i] = __float2bfloat16_rn(s);
+    }
+  } else {
+    const int nv = K / 8;
+    for (int idx = threadIdx.x; idx < kB * nv; idx += blockDim.x) {
+      const int b = idx / nv, v = idx - b * nv;
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (b0 + b < a.B) u = *reinterpret_cast<const uint4*>(a.x + (int64_t)(b0 + b) * K + v * 8);
+      *reinterpret_cast<uint4*>(xs + b * K + v * 8) = u;
+    }
+  }
+  __syncthreads();
+  if (!row_ok) return;
+  float acc[kB];
+#pragma unroll
+  for (int b = 0; b < kB; ++b) acc[b] = 0.f;
+#pragma unroll
+  for (int j = 0; j < kV; ++j) {
+    const int kk = lane * 8 + j * 256;
+    if (kk >= K) break;  // uniform per j across lanes only when K % 256 == 0; per lane otherwise
+    float wf[8];
+    Elt<__nv_bfloat16>::unpack(w[j], wf);
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      float xf[8];
+      Elt<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(xs + b * K + kk), xf);
+      float p0 = wf[0] * xf[0], p1 = wf[1] * xf[1];
+      p0 = fmaf(wf[2], xf[2], p0);
+      p1 = fmaf(wf[3], xf[3], p1);
+      p0 = fmaf(wf[4], xf[4], p0);
+      p1 = fmaf(wf[5], xf[5], p1);
+      p0 = fmaf(wf[6], xf[6], p0);
+      p1 = fmaf(wf[7], xf[7], p1);
+      acc[b] += p0 + p1;
+    }
+  }
+  const float bias = a.bias ? __bfloat162float(a.bias[n]) : 0.f;
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    const float h = warp_sum(acc[b]) + bias;
+    if (lane == b && b0 + b < a.B) {
+      float y = __bfloat162float(__float2bfloat16_rn(h));
+      if constexpr (kSilu) y = silu_exact(y);
+      a.y[(int64_t)(b0 + b) * a.N + n] = __float2bfloat16_rn(y);
+    }
+  }
+}
+
+template <int kB, int kV, bool kSinIn, bool kSilu>
+int launch_direct(const TembLayer& a, int b0, cudaStream_t st) {
+  const int64_t grid = cdiv(a.N, kDirectWarps);
+  if (cudaError_t e = launch_pdl(temb_direct_kernel<kB, kV, kSinIn, kSilu, !kSinIn>, dim3((unsigned)grid),
+                                 dim3(kDirectWarps * 32), 0, st, a, b0))
+    return launch_failed(e, "timestep_mlp");
+  return after_launch("temb_direct_kernel");
+}
+
+// The direct kernel for layers whose weights are at most kDirectBytes (and batch
+// chunks of at most kDirectMaxB rows): returns true when it took the layer.
+constexpr int64_t kDirectBytes = 32ll << 20;
+template <bool kSinIn, bool kSilu>
+bool try_direct(const TembLayer& a, cudaStream_t st, int& status) {
+  if ((int64_t)a.N * a.K * 2 > kDirectBytes || a.K > kMaxK) return false;
+  status = JO_OK;
+  for (int b0 = 0; b0 < a.B && status == JO_OK; b0 += kDirectMaxB) {  // one launch at the model's batch
+    const bool one = a.B - b0 == 1;
+    const int kv = (a.K + 255) / 256;
+    if (kv <= 1)
+      status = one ? launch_direct<1, 1, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 1, kSinIn, kSilu>(a, b0, st);
+    else if (kv <= 4)
+      status = one ? launch_direct<1, 4, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 4, kSinIn, kSilu>(a, b0, st);
+    else if (kv <= 12)
+      status = one ? launch_direct<1, 12, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 12, kSinIn, kSilu>(a, b0, st);
+    else
+      status = one ? launch_direct<1, 16, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 16, kSinIn, kSilu>(a, b0, st);
+  }
+  return true;
+}
+
 template <int kB, bool kSinIn, bool kSilu>
 int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, size_t smem, cudaStream_t st,
                const DeviceInfo* di) {
@@ -213,6 +334,11 @@ int launch_one(const TembLayer& a, const TembCfg& cfg, int b0, int64_t grid, siz
 
 template <bool kSinIn, bool kSilu>
 int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
+  // the time_proj layer (ModulateWan tables in its epilogue) always streams
+  if (kSilu && a.B <= kDirectMaxB) {
+    int s = JO_OK;
+    if (try_direct<kSinIn, kSilu>(a, st, s)) return s;
+  }
   for (int b0 = 0; b0 < a.B; b0 += kMaxB) {
     const int nb = std::min(kMaxB, a.B - b0);
     const int kb = nb <= 1 ? 1 : (nb <= 2 ? 2 : (nb <= 4 ? 4 : 8));
