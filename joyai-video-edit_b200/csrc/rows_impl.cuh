@@ -580,6 +580,10 @@ constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
 #ifndef JO_ROW_WARPS_CAP
 #define JO_ROW_WARPS_CAP 0
 #endif
+// Compile-time row length for 3072-wide 16-bit rows (1) or always the generic kernel (0).
+#ifndef JO_ROW_SPEC
+#define JO_ROW_SPEC 1
+#endif
 // threads per CTA by vectors per thread (register budget: 64 / 85 / 128 per thread);
 // JO_ROW_T12 sets it for 9-12 vectors per thread (3072-wide bf16 rows)
 #ifndef JO_ROW_T12
@@ -597,14 +601,18 @@ struct StagedCfg {
   uint32_t data_off;    // byte offset of slot 0
 };
 
-template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF>
+// kNV > 0: the row length in vectors is known at compile time (the launcher takes
+// it only when a.cols matches), so the bounds checks and shared-memory offsets of
+// the row loops fold into constants; the row group size follows from it.
+template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF, int kNV = 0>
 __global__ void __launch_bounds__(staged_threads(kVPT), 1)
     row_staged_kernel(RowArgs a, const StagedCfg cfg, unsigned int* fault) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   constexpr int V = Elt<T>::kVec, P = V / 2;
   using S = Sets<kF>;
+  constexpr int kG = kNV > 0 ? (kNV + 32 * kVPT - 1) / (32 * kVPT) : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = cfg.G, NG = cfg.warps / G, m = cfg.m;
+  const int G = kG > 0 ? kG : cfg.G, NG = cfg.warps / G, m = cfg.m;
   const int grp = warp / G, wg = warp % G;
   const int gl = wg * 32 + lane, GT = G * 32;  // thread within the group; group size
   const bool leader = gl == 0;
@@ -612,7 +620,7 @@ __global__ void __launch_bounds__(staged_threads(kVPT), 1)
   const int64_t r0 = (int64_t)blockIdx.x * per;
   const int64_t rend = r0 + per < a.rows ? r0 + per : a.rows;
   const int units = rend > r0 ? (int)(rend - r0) : 0;
-  const int nvec = (int)(a.cols / V);
+  const int nvec = kNV > 0 ? kNV : (int)(a.cols / V);
   const uint32_t row_bytes = (uint32_t)nvec * 16u;
   const uint32_t base = smem_u32(smem_raw);
   const uint32_t cache = base + cfg.cache_off;
@@ -849,10 +857,20 @@ inline bool row_vec_ok(const RowArgs& a, int esize) {
   return true;
 }
 
+// 3072-wide 16-bit rows (the model's hidden size, 384 vectors): one warp per row
+// (12 vectors per thread) or four-warp groups of residual rows (3 per thread)
+constexpr int kSpecNV = 384;
+template <typename T, int kVPT, int kPro>
+constexpr bool spec_ok() {
+  return JO_ROW_SPEC && sizeof(T) == 2 && (kVPT == 12 || (kVPT == 3 && kPro == kResidGate));
+}
+
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF>
 int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
-  auto kern = row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF>;
   constexpr int V = Elt<T>::kVec;
+  const bool spec = spec_ok<T, kVPT, kPro>() && a.cols / V == kSpecNV;
+  auto kern = spec ? row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF, spec_ok<T, kVPT, kPro>() ? kSpecNV : 0>
+                   : row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF, 0>;
   constexpr uint32_t kBudget = 216u * 1024u;
   const int nvec = (int)(a.cols / V);
   const uint32_t row_bytes = (uint32_t)(a.cols * sizeof(T)) * (kPro == kResidGate ? 2u : 1u);
@@ -901,8 +919,8 @@ int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   cfg.cache_off = (cfg.red_off + (uint32_t)(ng * 3 * kMaxG * 4) + 127u) & ~127u;
   cfg.data_off = cfg.cache_off + cache_bytes;
   const size_t smem = cfg.data_off + (size_t)ng * cfg.m * cfg.slot_bytes;
-  static std::atomic<uint64_t> reserved{0};
-  if (int s = reserve_smem((const void*)kern, 220 * 1024, reserved, di, "row kernel")) return s;
+  static std::atomic<uint64_t> reserved[2];  // generic and specialised kernels
+  if (int s = reserve_smem((const void*)kern, 220 * 1024, reserved[spec ? 1 : 0], di, "row kernel")) return s;
   // one CTA per SM whenever every SM gets a row: a short matrix (3600 rows: ~25
   // per SM) is spread over all SMs with each group's 1-3 rows in flight at once
   // (m above), rather than packed into fewer CTAs that leave SMs idle
