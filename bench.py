@@ -73,6 +73,9 @@ class Workload:
     name = ""
     desc = ""
     shape: dict = {}
+    # what the end-to-end leg calls: the op through the torch boundary, pinned host
+    # inputs copied in and results copied out on the same stream inside the timed region
+    e2e_api = "torch.ops.joyomni_ops op with pinned host inputs / outputs, copies inside the timed region"
 
     def algo_bytes(self) -> int:
         raise NotImplementedError
@@ -104,6 +107,8 @@ class QkvPack(Workload):
     name = "qkv_pack"
     desc = "qkv_norm_rope_pack: qkv [10800,9216] bf16 -> q/k/v [24,10800,128] (BASELINE configs[1])"
     L, H, D = 10800, 24, 128
+    e2e_api = ("torch.ops.joyomni_ops.qkv_norm_rope_pack_host (C ABI jo_qkv_norm_rope_pack_host): pinned host "
+               "buffers, uploads / pack / downloads overlapped by token chunks, all copies inside the timed region")
 
     def __init__(self):
         self.shape = {"tokens": self.L, "heads": self.H, "head_dim": self.D, "qkv": [self.L, 3 * self.H * self.D],
@@ -298,8 +303,13 @@ class Gemm(Workload):
         sb = torch.empty(self.N, dtype=torch.float32, device=dev)
         jo.sgl_per_token_quant_fp8(x["w"], wq, sb)  # per-output-channel weight quant
         st = dict(jo=jo, aq=aq, sa=sa, bq=wq.t(), sb=sb.view(1, -1))
-        d = self.step(st)
-        return dict(st, inputs={"aq": aq}, outputs={"d": d})
+        self._extra(st, seed)
+        out = self.step(st)
+        outs = {"d": out} if torch.is_tensor(out) else {f"o{i}": t for i, t in enumerate(out)}
+        return dict(st, inputs={"aq": aq}, outputs=outs)
+
+    def _extra(self, st, seed):
+        """Operands beyond A and B (set before the first step)."""
 
     def step(self, st):
         return st["jo"].fp8_scaled_mm(st["aq"], st["bq"], st["sa"], st["sb"], torch.bfloat16, None)
@@ -322,6 +332,46 @@ class Gemm(Workload):
     def cpu_step(self, x):
         # the reference's torch fallback: dequantised fp32 GEMM on the host cores
         return ((x["aq"].float() * x["sa"]) @ (x["bq"] * x["sb"])).to(BF)
+
+
+class GemmGelu(Gemm):
+    """The MLP's fc1 -> GELU-tanh -> per-token FP8 (dit.py:508-513) in one op: the FP8 GEMM
+    with bias, GELU and the row amax in its epilogue, then the quantisation pass."""
+
+    def __init__(self, name, M, N, K, desc):
+        super().__init__(name, M, N, K, desc)
+        self.shape = {**self.shape, "bias": "bf16 [N]", "out": "e4m3 [M, N] + fp32 [M, 1] (bf16 GELU workspace)"}
+
+    def algo_bytes(self):
+        # GEMM operands, the bf16 GELU written and read back once, the e4m3 result and scales
+        return self.M * self.K + self.K * self.N + 2 * self.N + 4 * 2 * self.M * self.N + self.M * self.N + 4 * (
+            2 * self.M + self.N)
+
+    def _extra(self, st, seed):
+        g = torch.Generator().manual_seed(seed + 1)
+        st["bias"] = (0.1 * torch.randn(self.N, generator=g)).to(BF).to(st["aq"].device)
+
+    def step(self, st):
+        return st["jo"].fp8_scaled_mm_gelu_quant(st["aq"], st["bq"], st["sa"], st["sb"], torch.bfloat16, st["bias"])
+
+    def e2e_step(self, st, host_in, host_out):
+        st["aq"].copy_(host_in["aq"], non_blocking=True)
+        q, s = self.step(st)
+        host_out["o0"].copy_(q, non_blocking=True)
+        host_out["o1"].copy_(s, non_blocking=True)
+
+    def make_cpu(self, seed):
+        x = super().make_cpu(seed)
+        g = torch.Generator().manual_seed(seed + 1)
+        x["bias"] = (0.1 * torch.randn(self.N, generator=g)).to(BF)
+        return x
+
+    def cpu_step(self, x):
+        from oracle import ops
+
+        # the reference's torch fallback: dequantised fp32 GEMM + bias, F.gelu, per-token quant
+        up = ((x["aq"].float() * x["sa"]) @ (x["bq"] * x["sb"]) + x["bias"].float()).to(BF)
+        return ops.per_token_quant_fp8(ops.gelu_tanh(up))
 
 
 class Temb(Workload):
@@ -507,6 +557,9 @@ def workloads():
                             "quant, configs[2]/[4])"),
         "gemm_qkv": Gemm("gemm_qkv", 10800, 9216, 3072, "FP8 GEMM QKV projection [10800,3072]x[3072,9216] (configs[3])"),
         "gemm_up": Gemm("gemm_up", 10800, 12288, 3072, "FP8 GEMM MLP-up [10800,3072]x[3072,12288] (configs[3])"),
+        "gemm_up_gelu_quant": GemmGelu("gemm_up_gelu_quant", 10800, 12288, 3072,
+                                       "FP8 GEMM MLP-up + bias -> GELU-tanh -> per-token FP8 [10800,3072]x[3072,12288] "
+                                       "(configs[3] GEMM with the block's MLP activation and down-projection quant)"),
         "chain": Chain(),
         "temb": Temb(),
     }
@@ -807,16 +860,14 @@ def run_headline(args, wl: Workload, world: int, rank: int, local: int, dev):
                      "traffic": profile_traffic(wl.name), "kernel_us": round(ms * 1e3, 2)},
         "e2e": {"value": round(world * B / (e2e_step_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_step_ms, 3),
-                "api": "torch.ops.joyomni_ops.qkv_norm_rope_pack_host (C ABI jo_qkv_norm_rope_pack_host): pinned "
-                       "host buffers, uploads / pack / downloads overlapped by token chunks, all copies inside the "
-                       "timed region"},
+                "api": wl.e2e_api},
         "gpu_launches": int(launches),
         "clocks": clk,
     }
 
 
 PER_OP = ["rmsnorm", "ln_mod", "gated_ln", "gelu", "silu_mul", "quant", "rmsnorm_quant", "gelu_quant", "gemm_qkv",
-          "gemm_up", "temb"]
+          "gemm_up", "gemm_up_gelu_quant", "temb"]
 
 
 def run_per_op(args, dev, local: int) -> dict:

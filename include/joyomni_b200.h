@@ -162,6 +162,24 @@ JO_API int jo_fp8_scaled_mm_gated_residual(void* d, int64_t ldd, const void* a, 
                                            const void* residual, int64_t ldr, const void* gate, int64_t m, int64_t n,
                                            int64_t k, int out_dtype, void* stream);
 
+/* The MLP's fc1 -> GELU -> per-token FP8 (dit.py:508-513: Fp8Linear, F.gelu
+ * tanh, then the next Fp8Linear's per-token quantisation, fp8_linear.py:38-43):
+ *   y = y_dtype(GELU_tanh(y_dtype((A.B) * sB[n] * sA[m] (+ bias[n]))))
+ *   out_s[m] = max(max_n |y[m,n]|, 1e-8) / 448; out_q = e4m3(y / out_s[m])
+ * GELU and the per-row amax run in the GEMM epilogue; a second kernel quantises
+ * y.  q and out_s equal jo_per_token_quant_fp8 applied to
+ * jo_gelu_tanh(jo_fp8_scaled_mm(...)) bit for bit.
+ * y: caller workspace [M, N] of y_dtype (row stride ldy), left holding the GELU
+ * output; amax: caller workspace of M uint32 (zeroed here on the stream);
+ * out_q: e4m3 [M, N] (row stride ldq, a multiple of 8 bytes, >= N); out_s:
+ * fp32 [M].  Other arguments as jo_fp8_scaled_mm; N > 0.  Three stream
+ * operations: a memset of amax, the GEMM, the quantisation. */
+JO_API int jo_fp8_scaled_mm_gelu_quant(void* out_q, int64_t ldq, float* out_s, void* y, int64_t ldy,
+                                       uint32_t* amax, const void* a, int64_t lda, const void* b,
+                                       int64_t ldb, const float* scale_a, const float* scale_b,
+                                       const void* bias, int64_t m, int64_t n, int64_t k, int y_dtype,
+                                       void* stream);
+
 /* ====================================================================== *
  *  New fused ops on the same path (no single reference kernel)
  * ====================================================================== */

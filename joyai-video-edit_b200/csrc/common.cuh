@@ -207,14 +207,58 @@ __device__ __forceinline__ float quant_clamp(float x, float scale) {
 }
 
 // GELU, tanh approximation: x * sigmoid(2u), u = sqrt(2/pi) * (x + 0.044715 x^3);
-// 0.5 * (1 + tanh(u)) == 1 / (1 + exp(-2u)) exactly.  The exp argument is
-// capped so that 1 + e stays finite (x / inf would lose the sign of -0).
+// 0.5 * (1 + tanh(u)) == 1 / (1 + e^(-2u)) exactly.  Every step is spelled out
+// (one rounding each) so that the scalar and the f32x2 forms below give the
+// same bits:  t = fma(0.044715, x^3, x);  z = min(-2 sqrt(2/pi) t, 80);
+// e = 2^(z log2(e)) with the hardware base-2 exponential (ex2.approx, relative
+// error about 2^-22); y = x * rcp(1 + e) with the hardware reciprocal
+// (rcp.approx, 1 ulp).  The cap keeps 1 + e <= 5.6e34, far from the flush-to-
+// zero range of the reciprocal, so y keeps the sign of x (also for -0).
+constexpr float kGeluC = 0.044715f;
+constexpr float kGeluNegK = -1.5957691216057308f;  // -2 * sqrt(2/pi)
+constexpr float kLog2E = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float v) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
 __device__ __forceinline__ float gelu_tanh_f(float x) {
-  constexpr float kTwoSqrt2OverPi = 1.5957691216057308f;  // 2 * sqrt(2/pi)
-  const float x3 = x * x * x;
-  const float z = -kTwoSqrt2OverPi * (x + 0.044715f * x3);
-  const float e = __expf(fminf(z, 80.f));
-  return __fdividef(x, 1.f + e);
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float t = __fmaf_rn(kGeluC, x3, x);
+  const float z = fminf(__fmul_rn(kGeluNegK, t), 80.f);
+  const float e = ex2_approx(__fmul_rn(z, kLog2E));
+  return __fmul_rn(x, rcp_approx(__fadd_rn(1.f, e)));
+}
+// Two elements at once: the same steps on the packed f32x2 pipe (half the
+// issue slots of the scalar form); the exponential and reciprocal stay scalar.
+__device__ __forceinline__ float2 gelu_tanh_f2(float2 x) {
+  const float2 x3 = __fmul2_rn(__fmul2_rn(x, x), x);
+  const float2 t = __ffma2_rn(make_float2(kGeluC, kGeluC), x3, x);
+  float2 z = __fmul2_rn(make_float2(kGeluNegK, kGeluNegK), t);
+  z = make_float2(fminf(z.x, 80.f), fminf(z.y, 80.f));
+  z = __fmul2_rn(z, make_float2(kLog2E, kLog2E));
+  const float2 d = __fadd2_rn(make_float2(1.f, 1.f), make_float2(ex2_approx(z.x), ex2_approx(z.y)));
+  return __fmul2_rn(x, make_float2(rcp_approx(d.x), rcp_approx(d.y)));
+}
+
+// GELU-tanh of one 16-byte vector of T, rounded to T (the tensor the unfused
+// chain materialises), two elements per step.
+template <typename T>
+__device__ __forceinline__ uint4 gelu_vec(const uint4& u) {
+  float f[Elt<T>::kVec];
+  Elt<T>::unpack(u, f);
+#pragma unroll
+  for (int e = 0; e < Elt<T>::kVec; e += 2) {
+    const float2 g = gelu_tanh_f2(make_float2(f[e], f[e + 1]));
+    f[e] = g.x;
+    f[e + 1] = g.y;
+  }
+  return Elt<T>::pack(f);
 }
 
 // 1/sqrt(v) rounded as torch's CPU rsqrt (IEEE sqrt, then IEEE reciprocal).

@@ -20,7 +20,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
-// gelu_tanh_f (common.cuh): x * sigmoid(2u), the identical form of
+// gelu_tanh_f / gelu_vec (common.cuh): x * sigmoid(2u), the identical form of
 // 0.5 * x * (1 + tanh(u)).
 
 __device__ __forceinline__ float silu_f(float a) {
@@ -47,11 +47,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t i = base + (int64_t)u * kThreads;
       if (i < nvec) {
-        float f[V];
-        Elt<T>::unpack(v[u], f);
-#pragma unroll
-        for (int e = 0; e < V; ++e) f[e] = gelu_tanh_f(f[e]);
-        st_global(out + i * V, Elt<T>::pack(f));
+        st_global(out + i * V, gelu_vec<T>(v[u]));
       }
     }
   }

@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "pipeline.cuh"
+#include "quant.cuh"
 
 namespace jo {
 namespace {
@@ -115,6 +116,7 @@ struct GemmArgs {
   const void* res;   // kEpiResid: residual [M, N] (row stride ldr), same dtype as D
   int64_t ldr;
   const void* gate;  // kEpiResid: gate [N], same dtype as D
+  uint32_t* amax;    // kEpiGelu: per-row max |GELU| as 16-bit magnitude bits (zeroed before)
   int m, n, k;
   int tiles_m, tiles_n;
   unsigned int* fault;
@@ -122,8 +124,11 @@ struct GemmArgs {
 
 // Epilogue variants: + bias[n]; gated residual D = res + gate[n] * (GEMM result)
 // (torch.addcmul(res, x, gate) of sgl_fused_ops.py:302-305 applied to the fp32
-// result, dit.py:536-538) instead of rounding the product to D's dtype first.
-enum GemmEpi { kEpiBias = 1, kEpiResid = 2 };
+// result, dit.py:536-538) instead of rounding the product to D's dtype first;
+// GELU-tanh of the rounded result (the MLP's fc1 -> GELU, dit.py:508-513) with
+// a per-row running max of |GELU| for the per-token FP8 quantisation that
+// follows.
+enum GemmEpi { kEpiBias = 1, kEpiResid = 2, kEpiGelu = 4 };
 
 template <typename OutT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -134,6 +139,65 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
 template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return pack_f16x2(a, b);
+}
+
+// Epilogue of one thread's 32 accumulator columns [n0, n0 + 32) of its row:
+// (acc * sB) * sA (+ bias) in fp32, then either the gated residual or, for
+// kEpiGelu, the rounding to OutT that the Linear's output holds, GELU-tanh of
+// that value rounded to OutT again (the elementwise kernel's arithmetic) and a
+// running |GELU| maximum; stored 16 bytes at a time.
+template <typename OutT, int kEpi>
+__device__ __forceinline__ void epi_chunk(const uint32_t* r, int n0, const GemmArgs& args, float s_a, bool row_ok,
+                                          OutT* drow, const OutT* rrow, uint32_t& amax16) {
+  constexpr bool kBias = (kEpi & kEpiBias) != 0, kResid = (kEpi & kEpiResid) != 0;
+  constexpr bool kGelu = (kEpi & kEpiGelu) != 0;
+  const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
+  const OutT* gate = reinterpret_cast<const OutT*>(args.gate);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
+    const int ng = n0 + g * 8;
+    if (ng >= args.n) break;
+    const float4 sb0 = __ldg(reinterpret_cast<const float4*>(args.sb + ng));
+    const float4 sb1 = __ldg(reinterpret_cast<const float4*>(args.sb + ng + 4));
+    const float sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
+    float bv[8];
+    if constexpr (kBias) {
+      float t[8];
+      Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(bias + ng)), t);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bv[e] = t[e];
+    }
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float t = __uint_as_float(r[g * 8 + e]) * sb[e];
+      o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
+    }
+    if (row_ok) {
+      if constexpr (kResid) {
+        float rv[8], gv[8];
+        // plain (coherent) load: D may alias the residual
+        Elt<OutT>::unpack(*reinterpret_cast<const uint4*>(rrow + ng), rv);
+        Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(gate + ng)), gv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = fmaf(gv[e], o[e], rv[e]);
+      }
+      uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
+                           pack2<OutT>(o[6], o[7]));
+      if constexpr (kGelu) {
+        v = gelu_vec<OutT>(v);
+        amax16 = absmax_u16x2(absmax_u16x2(amax16, v.x), v.y);
+        amax16 = absmax_u16x2(absmax_u16x2(amax16, v.z), v.w);
+      }
+      *reinterpret_cast<uint4*>(drow + ng) = v;
+    }
+  }
+}
+// One atomic per thread and tile: the row's |GELU| maximum over its columns.
+template <int kEpi>
+__device__ __forceinline__ void epi_row_done(const GemmArgs& args, int row, bool row_ok, uint32_t amax16) {
+  if constexpr ((kEpi & kEpiGelu) != 0)
+    if (row_ok) atomicMax(args.amax + row, max(amax16 & 0xffffu, amax16 >> 16));
 }
 
 template <typename OutT, int kEpi>
@@ -259,10 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
-    constexpr bool kBias = (kEpi & kEpiBias) != 0, kResid = (kEpi & kEpiResid) != 0;
     OutT* D = reinterpret_cast<OutT*>(args.d);
-    const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
-    const OutT* gate = reinterpret_cast<const OutT*>(args.gate);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
       if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
@@ -273,47 +334,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
       const OutT* rrow = reinterpret_cast<const OutT*>(args.res) + (int64_t)(row_ok ? row : 0) * args.ldr;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kBN);
+      uint32_t amax16 = 0;
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         const int n0 = tn * kBN + c * 32;
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         if (n0 >= args.n) continue;  // whole chunk past N (uniform across the warp)
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
-          const int ng = n0 + g * 8;
-          if (ng >= args.n) break;
-          const float4 sb0 = __ldg(reinterpret_cast<const float4*>(args.sb + ng));
-          const float4 sb1 = __ldg(reinterpret_cast<const float4*>(args.sb + ng + 4));
-          const float sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
-          float bv[8];
-          if constexpr (kBias) {
-            float t[8];
-            Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(bias + ng)), t);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) bv[e] = t[e];
-          }
-          float o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float t = __uint_as_float(r[g * 8 + e]) * sb[e];
-            o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
-          }
-          if (row_ok) {
-            if constexpr (kResid) {
-              float rv[8], gv[8];
-              // plain (coherent) load: D may alias the residual
-              Elt<OutT>::unpack(*reinterpret_cast<const uint4*>(rrow + ng), rv);
-              Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(gate + ng)), gv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] = fmaf(gv[e], o[e], rv[e]);
-            }
-            uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
-                                 pack2<OutT>(o[6], o[7]));
-            *reinterpret_cast<uint4*>(drow + ng) = v;
-          }
-        }
+        epi_chunk<OutT, kEpi>(r, n0, args, s_a, row_ok, drow, rrow, amax16);
       }
+      epi_row_done<kEpi>(args, row, row_ok, amax16);
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
       if (++acc == 2) {
@@ -539,10 +569,7 @@ __global__ void __launch_bounds__(kP_Threads, 1)
     const int q = warp & 3, half = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    constexpr bool kBias = (kEpi & kEpiBias) != 0, kResid = (kEpi & kEpiResid) != 0;
     OutT* D = reinterpret_cast<OutT*>(args.d);
-    const OutT* bias = reinterpret_cast<const OutT*>(args.bias);
-    const OutT* gate = reinterpret_cast<const OutT*>(args.gate);
     for (int tile = cluster; tile < num_tiles; tile += nclusters) {
       const int tm = tile / args.tiles_n, tn = tile - tm * args.tiles_n;
       if (!mbar_wait(tfull_bar(acc), acc_phase, fault)) break;
@@ -553,47 +580,16 @@ __global__ void __launch_bounds__(kP_Threads, 1)
       OutT* drow = D + (int64_t)(row_ok ? row : 0) * args.ldd;
       const OutT* rrow = reinterpret_cast<const OutT*>(args.res) + (int64_t)(row_ok ? row : 0) * args.ldr;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * kP_BN);
+      uint32_t amax16 = 0;
 #pragma unroll 1
       for (int c = half * (kP_BN / 64); c < (half + 1) * (kP_BN / 64); ++c) {
         const int n0 = tn * kP_BN + c * 32;
         uint32_t r[32];
         tmem_ld32(t_row + (uint32_t)(c * 32), r);
         if (n0 >= args.n) continue;  // whole chunk past N (uniform across the warp)
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {  // 8 columns per 16-byte store
-          const int ng = n0 + g * 8;
-          if (ng >= args.n) break;
-          const float4 sb0 = __ldg(reinterpret_cast<const float4*>(args.sb + ng));
-          const float4 sb1 = __ldg(reinterpret_cast<const float4*>(args.sb + ng + 4));
-          const float sb[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
-          float bv[8];
-          if constexpr (kBias) {
-            float t[8];
-            Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(bias + ng)), t);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) bv[e] = t[e];
-          }
-          float o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float t = __uint_as_float(r[g * 8 + e]) * sb[e];
-            o[e] = kBias ? fmaf(s_a, t, bv[e]) : s_a * t;
-          }
-          if (row_ok) {
-            if constexpr (kResid) {
-              float rv[8], gv[8];
-              // plain (coherent) load: D may alias the residual
-              Elt<OutT>::unpack(*reinterpret_cast<const uint4*>(rrow + ng), rv);
-              Elt<OutT>::unpack(__ldg(reinterpret_cast<const uint4*>(gate + ng)), gv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] = fmaf(gv[e], o[e], rv[e]);
-            }
-            uint4 v = make_uint4(pack2<OutT>(o[0], o[1]), pack2<OutT>(o[2], o[3]), pack2<OutT>(o[4], o[5]),
-                                 pack2<OutT>(o[6], o[7]));
-            *reinterpret_cast<uint4*>(drow + ng) = v;
-          }
-        }
+        epi_chunk<OutT, kEpi>(r, n0, args, s_a, row_ok, drow, rrow, amax16);
       }
+      epi_row_done<kEpi>(args, row, row_ok, amax16);
       tc_fence_before();
       if (leader)
         mbar_arrive(tempty_bar(acc));
@@ -704,6 +700,64 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArg
   return after_launch("fp8_gemm_pair_kernel");
 }
 
+// ------------------------------------------------------------------ GELU -> FP8
+// Second pass of the MLP's fc1 -> GELU -> per-token FP8: the GEMM epilogue has
+// stored y = GELU(fc1) as OutT and the per-row max |y| (16-bit magnitude bits);
+// this pass is the quantisation alone, with the row quant kernels' arithmetic
+// (scale = max(amax, 1e-8) / 448, q = e4m3(y / scale) with the correctly rounded
+// quotient, satfinite), so q and scale equal sgl_per_token_quant_fp8(y) bit for
+// bit.  One CTA per row; each thread holds its kApplyVPT 16-byte vectors in
+// flight before converting them.
+constexpr int kApplyThreads = 256;
+constexpr int kApplyVPT = 6;  // 12288 bf16 = 1536 vectors per row: one pass
+
+template <typename T>
+__global__ void __launch_bounds__(kApplyThreads) gelu_quant_apply_kernel(const T* __restrict__ y, int64_t ldy,
+                                                                         const uint32_t* __restrict__ amax,
+                                                                         uint8_t* __restrict__ q, int64_t ldq,
+                                                                         float* __restrict__ s_out, int nvec) {
+  pdl_wait();  // y and amax are the GEMM's outputs
+  const int64_t row = blockIdx.x;
+  const float s = quant_scale(bits16_to_f<T>(amax[row]));
+  const float2 ns2 = f2(-s), rc2 = f2(__frcp_rn(s));
+  const uint8_t* yr = reinterpret_cast<const uint8_t*>(y + row * ldy);
+  uint8_t* qr = q + row * ldq;
+  for (int base = threadIdx.x; base < nvec; base += kApplyThreads * kApplyVPT) {
+    uint4 v[kApplyVPT];
+#pragma unroll
+    for (int u = 0; u < kApplyVPT; ++u) {
+      const int idx = base + u * kApplyThreads;
+      if (idx < nvec) v[u] = ld_stream(yr + (int64_t)idx * 16);
+    }
+#pragma unroll
+    for (int u = 0; u < kApplyVPT; ++u) {
+      const int idx = base + u * kApplyThreads;
+      if (idx >= nvec) continue;
+      float2 p[4], qq[4];
+      to_pairs<T>(v[u], p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) qq[e] = div2_ms(p[e], ns2, rc2);
+      const uint32_t w0 = ((uint32_t)e4m3x2(qq[0].x, qq[0].y) | ((uint32_t)e4m3x2(qq[1].x, qq[1].y) << 16)) |
+                          e4m3_signs(v[u].x, v[u].y);
+      const uint32_t w1 = ((uint32_t)e4m3x2(qq[2].x, qq[2].y) | ((uint32_t)e4m3x2(qq[3].x, qq[3].y) << 16)) |
+                          e4m3_signs(v[u].z, v[u].w);
+      *reinterpret_cast<uint2*>(qr + (int64_t)idx * 8) = make_uint2(w0, w1);
+    }
+  }
+  if (threadIdx.x == 0) s_out[row] = s;
+  pdl_trigger();
+}
+
+template <typename T>
+int launch_gelu_quant_apply(uint8_t* q, int64_t ldq, float* s, const void* y, int64_t ldy, const uint32_t* amax,
+                            int64_t m, int64_t n, cudaStream_t st) {
+  auto kern = gelu_quant_apply_kernel<T>;
+  if (cudaError_t e = launch_pdl(kern, dim3((unsigned)m), dim3(kApplyThreads), 0, st, reinterpret_cast<const T*>(y),
+                                 ldy, amax, q, ldq, s, (int)(n / 8)))
+    return launch_failed(e, "fp8_scaled_mm_gelu_quant");
+  return after_launch("gelu_quant_apply_kernel");
+}
+
 }  // namespace
 }  // namespace jo
 
@@ -722,7 +776,7 @@ int dispatch_gemm(bool pair, int out_dtype, const CUtensorMap& ma, const CUtenso
 
 int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
                const float* scale_a, const float* scale_b, const void* bias, const void* res, int64_t ldr,
-               const void* gate, int64_t m, int64_t n, int64_t k, int out_dtype, void* stream) {
+               const void* gate, uint32_t* amax, int64_t m, int64_t n, int64_t k, int out_dtype, void* stream) {
   const DeviceInfo* di;
   if (int s = device_info(&di)) return s;
   if (m < 0 || n < 0 || k < 0) return fail(JO_ERR_SHAPE, "%s: negative size", op);
@@ -750,6 +804,7 @@ int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda,
   g.res = res;
   g.ldr = ldr;
   g.gate = gate;
+  g.amax = amax;
   g.m = (int)m;
   g.n = (int)n;
   g.k = (int)k;
@@ -758,12 +813,15 @@ int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda,
   g.fault = di->fault;
   if ((int64_t)g.tiles_m * g.tiles_n > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many tiles", op);
   cudaStream_t st = (cudaStream_t)stream;
-  const int epi = (bias ? kEpiBias : 0) | (res ? kEpiResid : 0);
+  const int epi = (bias ? kEpiBias : 0) | (res ? kEpiResid : 0) | (amax ? kEpiGelu : 0);
   switch (epi) {
     case 0: return dispatch_gemm<0>(pair, out_dtype, ma, mb, g, st, di);
     case kEpiBias: return dispatch_gemm<kEpiBias>(pair, out_dtype, ma, mb, g, st, di);
     case kEpiResid: return dispatch_gemm<kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
-    default: return dispatch_gemm<kEpiBias | kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
+    case kEpiBias | kEpiResid: return dispatch_gemm<kEpiBias | kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
+    case kEpiGelu: return dispatch_gemm<kEpiGelu>(pair, out_dtype, ma, mb, g, st, di);
+    case kEpiBias | kEpiGelu: return dispatch_gemm<kEpiBias | kEpiGelu>(pair, out_dtype, ma, mb, g, st, di);
+    default: return fail(JO_ERR_INVALID, "%s: residual and GELU epilogues are exclusive", op);
   }
 }
 
@@ -777,8 +835,8 @@ extern "C" {
 int jo_fp8_scaled_mm(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
                      const float* scale_a, const float* scale_b, const void* bias, int64_t m, int64_t n,
                      int64_t k, int out_dtype, void* stream) {
-  return gemm_entry("fp8_scaled_mm", d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, nullptr, 0, nullptr, m, n, k,
-                    out_dtype, stream);
+  return gemm_entry("fp8_scaled_mm", d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, nullptr, 0, nullptr, nullptr, m,
+                    n, k, out_dtype, stream);
 }
 
 int jo_fp8_scaled_mm_gated_residual(void* d, int64_t ldd, const void* a, int64_t lda, const void* b, int64_t ldb,
@@ -789,8 +847,31 @@ int jo_fp8_scaled_mm_gated_residual(void* d, int64_t ldd, const void* a, int64_t
   if (!residual || !gate) return fail(JO_ERR_INVALID, "%s: null residual or gate", op);
   if (ldr < n || ldr % 8) return fail(JO_ERR_ALIGN, "%s: residual row stride must be >= N and a multiple of 8", op);
   if (!aligned16(residual) || !aligned16(gate)) return fail(JO_ERR_ALIGN, "%s: residual and gate must be 16-byte aligned", op);
-  return gemm_entry(op, d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, residual, ldr, gate, m, n, k, out_dtype,
-                    stream);
+  return gemm_entry(op, d, ldd, a, lda, b, ldb, scale_a, scale_b, bias, residual, ldr, gate, nullptr, m, n, k,
+                    out_dtype, stream);
+}
+
+int jo_fp8_scaled_mm_gelu_quant(void* out_q, int64_t ldq, float* out_s, void* y, int64_t ldy, uint32_t* amax,
+                                const void* a, int64_t lda, const void* b, int64_t ldb, const float* scale_a,
+                                const float* scale_b, const void* bias, int64_t m, int64_t n, int64_t k,
+                                int y_dtype, void* stream) {
+  const char* op = "fp8_scaled_mm_gelu_quant";
+  if (m < 0 || n < 0) return fail(JO_ERR_SHAPE, "%s: negative size", op);
+  if (m == 0) return JO_OK;
+  if (n == 0) return fail(JO_ERR_SHAPE, "%s: N must be positive (per-token amax of an empty row)", op);
+  if (m > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: size too large", op);
+  if (!out_q || !out_s || !y || !amax) return fail(JO_ERR_INVALID, "%s: null output or workspace", op);
+  if (ldq < n || ldq % 8 || (reinterpret_cast<uintptr_t>(out_q) & 7))
+    return fail(JO_ERR_ALIGN, "%s: out_q must be 8-byte aligned with a row stride >= N, a multiple of 8", op);
+  if (reinterpret_cast<uintptr_t>(amax) & 3) return fail(JO_ERR_ALIGN, "%s: amax workspace must be 4-byte aligned", op);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)m * sizeof(uint32_t), st))
+    return launch_failed(e, "fp8_scaled_mm_gelu_quant (amax reset)");
+  if (int s = gemm_entry(op, y, ldy, a, lda, b, ldb, scale_a, scale_b, bias, nullptr, 0, nullptr, amax, m, n, k,
+                         y_dtype, stream))
+    return s;
+  return y_dtype == JO_BF16 ? launch_gelu_quant_apply<__nv_bfloat16>((uint8_t*)out_q, ldq, out_s, y, ldy, amax, m, n, st)
+                            : launch_gelu_quant_apply<__half>((uint8_t*)out_q, ldq, out_s, y, ldy, amax, m, n, st);
 }
 
 }  // extern "C"

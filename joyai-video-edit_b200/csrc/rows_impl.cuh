@@ -21,6 +21,7 @@
 // shapes that break 16-byte alignment take a scalar block-per-row path.
 #pragma once
 #include "pipeline.cuh"
+#include "quant.cuh"
 #include "rows_decl.cuh"
 
 namespace jo {
@@ -105,15 +106,6 @@ __device__ __forceinline__ uint4 resid_vec(const RowArgs& a, int64_t row, int id
   return h;
 }
 
-// GELU-tanh of one vector, rounded to T (the tensor the unfused chain materialises).
-template <typename T>
-__device__ __forceinline__ uint4 gelu_vec(const uint4& u) {
-  float f[Elt<T>::kVec];
-  Elt<T>::unpack(u, f);
-#pragma unroll
-  for (int e = 0; e < Elt<T>::kVec; ++e) f[e] = gelu_tanh_f(f[e]);
-  return Elt<T>::pack(f);
-}
 
 // kHDone: the caller already formed h (kResidGate) into raw and stored it.
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, bool kWarp, bool kHDone = false>
@@ -176,10 +168,25 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
   const T* bet = reinterpret_cast<const T*>(a.beta);
   const T* scr = has_mod ? reinterpret_cast<const T*>(a.scale) + row * a.mod_stride : nullptr;
   const T* shr = has_mod ? reinterpret_cast<const T*>(a.shift) + row * a.mod_stride : nullptr;
+  // |y| maximum: on the packed 16-bit patterns for bf16/fp16 (sign cleared,
+  // unsigned order = magnitude order), as floats for fp32
+  constexpr bool k16 = V == 8;
   float amax = 0.f;
+  uint32_t amax16 = 0;
+  // no norm and no affine / modulation operand: y is the row itself (quant, GELU -> quant)
+  const bool ident = kNorm == kNoNorm && !has_g && !has_b && !has_mod;
 #pragma unroll
   for (int i = 0; i < kVPT; ++i) {
     const int idx = g + i * G;
+    if constexpr (k16 && kEpi == kQuantY) {
+      if (ident) {
+        if (idx < nvec) {
+          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].x), raw[i].y);
+          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].z), raw[i].w);
+        }
+        continue;
+      }
+    }
     if (idx < nvec) {
       float f[V], fg[V], fb[V], fs[V], fh[V], y[V];
       Elt<T>::unpack(raw[i], f);
@@ -198,30 +205,43 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
         st_global(orow + (int64_t)idx * V, Elt<T>::pack(y));
       } else {
         raw[i] = Elt<T>::pack(y);  // y rounded to T, as the unfused chain materialises it
-        float r[V];
-        Elt<T>::unpack(raw[i], r);
+        if constexpr (k16) {
+          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].x), raw[i].y);
+          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].z), raw[i].w);
+        } else {
+          float r[V];
+          Elt<T>::unpack(raw[i], r);
 #pragma unroll
-        for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(r[j]));
+          for (int j = 0; j < V; ++j) amax = fmaxf(amax, fabsf(r[j]));
+        }
       }
     }
   }
   if constexpr (kEpi == kQuantY) {
+    if constexpr (k16) amax = bits16_to_f<T>(max(amax16 & 0xffffu, amax16 >> 16));
     const float s = quant_scale(row_reduce_max<kWarp>(amax, smem));
     uint8_t* qrow = a.out_q + row * a.q_stride;
+    // 16-bit rows: the correctly rounded quotient from RN(1/s) (div2_ms) with the
+    // signs of -0 restored on the bytes, as the staged path; fp32: IEEE division
+    const float2 ns2 = f2(-s), rc2 = f2(__frcp_rn(s));
 #pragma unroll
     for (int i = 0; i < kVPT; ++i) {
       const int idx = g + i * G;
       if (idx < nvec) {
-        float r[V];
-        Elt<T>::unpack(raw[i], r);
-        if constexpr (V == 8) {
+        if constexpr (k16) {
+          float2 p[4], q[4];
+          to_pairs<T>(raw[i], p);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) q[e] = div2_ms(p[e], ns2, rc2);
           uint2 o;
-          o.x = (uint32_t)e4m3x2(quant_clamp(r[0], s), quant_clamp(r[1], s)) |
-                ((uint32_t)e4m3x2(quant_clamp(r[2], s), quant_clamp(r[3], s)) << 16);
-          o.y = (uint32_t)e4m3x2(quant_clamp(r[4], s), quant_clamp(r[5], s)) |
-                ((uint32_t)e4m3x2(quant_clamp(r[6], s), quant_clamp(r[7], s)) << 16);
+          o.x = ((uint32_t)e4m3x2(q[0].x, q[0].y) | ((uint32_t)e4m3x2(q[1].x, q[1].y) << 16)) |
+                e4m3_signs(raw[i].x, raw[i].y);
+          o.y = ((uint32_t)e4m3x2(q[2].x, q[2].y) | ((uint32_t)e4m3x2(q[3].x, q[3].y) << 16)) |
+                e4m3_signs(raw[i].z, raw[i].w);
           *reinterpret_cast<uint2*>(qrow + (int64_t)idx * 8) = o;
         } else {
+          float r[V];
+          Elt<T>::unpack(raw[i], r);
           uint32_t o = (uint32_t)e4m3x2(quant_clamp(r[0], s), quant_clamp(r[1], s)) |
                        ((uint32_t)e4m3x2(quant_clamp(r[2], s), quant_clamp(r[3], s)) << 16);
           *reinterpret_cast<uint32_t*>(qrow + (int64_t)idx * 4) = o;
@@ -230,77 +250,6 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
     }
     if (g == 0) a.out_s[row] = s;
   }
-}
-
-// ------------------------------------------------------------------ packed math
-// f32x2 helpers for the staged path: a 16-byte vector of T as V/2 float pairs.
-template <typename T>
-__device__ __forceinline__ void to_pairs(const uint4& u, float2* p) {
-  float f[Elt<T>::kVec];
-  Elt<T>::unpack(u, f);
-#pragma unroll
-  for (int e = 0; e < Elt<T>::kVec / 2; ++e) p[e] = make_float2(f[2 * e], f[2 * e + 1]);
-}
-template <typename T>
-__device__ __forceinline__ uint4 from_pairs(const float2* p) {
-  float f[Elt<T>::kVec];
-#pragma unroll
-  for (int e = 0; e < Elt<T>::kVec / 2; ++e) {
-    f[2 * e] = p[e].x;
-    f[2 * e + 1] = p[e].y;
-  }
-  return Elt<T>::pack(f);
-}
-__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
-
-// Correctly rounded x / s from the correctly rounded reciprocal rc = RN(1/s):
-// q0 = RN(x*rc), r = x - q0*s (exact with an FMA), q = RN(q0 + r*rc).
-// Markstein, "Computation of elementary functions on the IBM RISC System/6000
-// processor" (IBM J. Res. Dev. 34(1), 1990), Theorem 1; valid while nothing
-// over- or underflows, which holds for |q| >= 2^-10, the only range where an
-// e4m3 byte depends on the quotient.
-// The quotient takes the sign of x (s > 0): copied back explicitly because the
-// correction step turns x = -0 into (+0) + (-0) = +0.
-__device__ __forceinline__ float2 div2_markstein(float2 x, float2 s, float2 rc) {
-  const float2 q0 = __fmul2_rn(x, rc);
-  const float2 r = __ffma2_rn(q0, make_float2(-s.x, -s.y), x);
-  const float2 q = __ffma2_rn(r, rc, q0);
-  return make_float2(copysignf(q.x, x.x), copysignf(q.y, x.y));
-}
-// The same quotient without the sign copy (ns = -s): for 16-bit inputs the
-// sign of x = -0 is restored on the packed e4m3 bytes instead (e4m3_signs),
-// one byte permute for four elements.
-__device__ __forceinline__ float2 div2_ms(float2 x, float2 ns, float2 rc) {
-  const float2 q0 = __fmul2_rn(x, rc);
-  const float2 r = __ffma2_rn(q0, ns, x);
-  return __ffma2_rn(r, rc, q0);
-}
-// Sign bits of the four 16-bit elements of words (w0, w1), at bit 7 of the
-// byte each element's e4m3 code occupies.  OR-ing them in is exact: a nonzero
-// quotient already carries its sign, a zero one gets the sign of x.
-__device__ __forceinline__ uint32_t e4m3_signs(uint32_t w0, uint32_t w1) {
-  return __byte_perm(w0, w1, 0x7531) & 0x80808080u;
-}
-// Running |x| maximum over packed 16-bit floats: bf16 and fp16 magnitudes
-// order exactly as their bit patterns with the sign cleared (unsigned).
-__device__ __forceinline__ uint32_t absmax_u16x2(uint32_t m, uint32_t w) {
-  uint32_t r;
-  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w & 0x7fff7fffu));
-  return r;
-}
-template <typename T>
-__device__ __forceinline__ float bits16_to_f(uint32_t h);
-template <>
-__device__ __forceinline__ float bits16_to_f<__nv_bfloat16>(uint32_t h) {
-  return __uint_as_float(h << 16);
-}
-template <>
-__device__ __forceinline__ float bits16_to_f<__half>(uint32_t h) {
-  return __half2float(__ushort_as_half((unsigned short)h));
-}
-template <>
-__device__ __forceinline__ float bits16_to_f<float>(uint32_t) {
-  return 0.f;
 }
 
 // Feature bits of a staged row op (compile-time, no per-element branches).
@@ -589,6 +538,11 @@ constexpr uint32_t kRowInflightSm = JO_ROW_INFLIGHT_SM;
 #ifndef JO_ROW_T12
 #define JO_ROW_T12 512
 #endif
+// GELU rows wider than 512 vectors (the MLP activation's 12288 bf16) through the
+// staged kernel in 4-warp groups (1) or the block path (0).
+#ifndef JO_ROW_WIDE
+#define JO_ROW_WIDE 0
+#endif
 constexpr int staged_threads(int vpt) { return vpt <= 4 ? 1024 : (vpt <= 8 ? 768 : (vpt <= 12 ? JO_ROW_T12 : 512)); }
 
 struct StagedCfg {
@@ -858,18 +812,22 @@ inline bool row_vec_ok(const RowArgs& a, int esize) {
 }
 
 // 3072-wide 16-bit rows (the model's hidden size, 384 vectors): one warp per row
-// (12 vectors per thread) or four-warp groups of residual rows (3 per thread)
+// (12 vectors per thread) or four-warp groups of residual rows (3 per thread).
+// Not for single-input LayerNorm + modulate: fully unrolled, it reaches the
+// 128-register cap and spills (measured 25.6 us against 24.7 us unspecialised).
 constexpr int kSpecNV = 384;
-template <typename T, int kVPT, int kPro>
+template <typename T, int kVPT, int kNorm, int kPro, int kF>
 constexpr bool spec_ok() {
-  return JO_ROW_SPEC && sizeof(T) == 2 && (kVPT == 12 || (kVPT == 3 && kPro == kResidGate));
+  return JO_ROW_SPEC && sizeof(T) == 2 && (kVPT == 12 || (kVPT == 3 && kPro == kResidGate)) &&
+         !(kNorm == kLayer && kPro != kResidGate && (kF & kFMod) != 0);
 }
 
 template <typename T, int kVPT, int kNorm, int kPro, int kEpi, int kF>
 int launch_staged_f(const RowArgs& a, cudaStream_t st, const DeviceInfo* di) {
   constexpr int V = Elt<T>::kVec;
-  const bool spec = spec_ok<T, kVPT, kPro>() && a.cols / V == kSpecNV;
-  auto kern = spec ? row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF, spec_ok<T, kVPT, kPro>() ? kSpecNV : 0>
+  constexpr bool kSpec = spec_ok<T, kVPT, kNorm, kPro, kF>();
+  const bool spec = kSpec && a.cols / V == kSpecNV;
+  auto kern = spec ? row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF, kSpec ? kSpecNV : 0>
                    : row_staged_kernel<T, kVPT, kNorm, kPro, kEpi, kF, 0>;
   constexpr uint32_t kBudget = 216u * 1024u;
   const int nvec = (int)(a.cols / V);
@@ -978,10 +936,9 @@ int launch_rows_t(const RowArgs& a, cudaStream_t st) {
   if (int s = device_info(&di)) return s;
   if (row_vec_ok(a, sizeof(T))) {
     const int nvec = (int)(a.cols / V);
-    // staged rows: up to 512 vectors (4096 bf16) per warp-owned row, residual rows up to
-    // 512 vectors in groups of up to 4 warps, and wider single-input rows (up to 2048
-    // vectors: the MLP activation's 12288 bf16) in groups of 2-4 warps
-    const int max_staged = kPro == kResidGate ? 32 * 16 : 4 * 32 * 16;
+    // staged rows: up to 512 vectors (4096 bf16); wider GELU rows (the MLP
+    // activation's 12288 bf16) too when JO_ROW_WIDE is set, else the block path.
+    const int max_staged = JO_ROW_WIDE && kPro == kGeluX ? 4 * 32 * 12 : 32 * 16;
     if (nvec <= max_staged && staged_operands_ok(a, kPro)) {
 #define JO_STAGED(VPT) return launch_staged<T, VPT, kNorm, kPro, kEpi>(a, st, di)
       // vectors per thread: one warp per row, or (residual + x rows) the
@@ -989,7 +946,7 @@ int launch_rows_t(const RowArgs& a, cudaStream_t st) {
       const bool split = kPro == kResidGate || (JO_ROW_G2 >= 1 && kEpi == kQuantY && kNorm != kNoNorm) ||
                          (JO_ROW_G2 >= 2 && kNorm != kNoNorm);
       int G = !split || nvec <= 128 ? 1 : (kPro != kResidGate || nvec <= 256 ? 2 : 4);
-      if (kPro != kResidGate && nvec > 32 * 16) G = nvec <= 2 * 32 * 12 ? 2 : 4;  // <= 12 (16) vectors per thread
+      if (nvec > 32 * 16) G = 4;  // wide GELU rows: 12 vectors per thread
       const int vpt = (nvec + 32 * G - 1) / (32 * G);
       if (vpt <= 2) JO_STAGED(2);
       if (vpt <= 3) JO_STAGED(3);

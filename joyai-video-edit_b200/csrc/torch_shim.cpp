@@ -395,11 +395,10 @@ torch::Tensor fp8_scaled_mm(const torch::Tensor& mat_a, const torch::Tensor& mat
 }
 
 // ------------------------------------------------------------------ new fused ops
-// fp8_scaled_mm + torch.addcmul(residual, ., gate) in the GEMM epilogue (dit.py:536-538).
-torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const torch::Tensor& mat_b,
-                                           const torch::Tensor& scales_a, const torch::Tensor& scales_b,
-                                           const torch::ScalarType& out_dtype, const c10::optional<torch::Tensor>& bias,
-                                           const torch::Tensor& residual, const torch::Tensor& gate) {
+// Operand checks of the fused FP8 GEMMs (fp8_scaled_mm's contract, in fewer messages).
+void check_fused_gemm_operands(const torch::Tensor& mat_a, const torch::Tensor& mat_b, const torch::Tensor& scales_a,
+                               const torch::Tensor& scales_b, const torch::ScalarType& out_dtype,
+                               const c10::optional<torch::Tensor>& bias) {
   TORCH_CHECK(mat_a.is_cuda() && mat_b.is_cuda(), "mat_a and mat_b must be CUDA tensors");
   TORCH_CHECK(mat_a.dim() == 2 && mat_b.dim() == 2, "mat_a and mat_b must be 2D tensors");
   TORCH_CHECK(mat_a.stride(1) == 1, "mat_a must be a row major tensor");
@@ -418,12 +417,20 @@ torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const tor
   check_dev(scales_a, mat_a, "scales_a");
   check_dev(scales_b, mat_a, "scales_b");
   check_dev(bias, mat_a, "bias");
-  check_dev(residual, mat_a, "residual");
-  check_dev(gate, mat_a, "gate");
   if (bias) {
     TORCH_CHECK(bias->numel() == mat_b.size(1) && bias->is_contiguous() && bias->dtype() == out_dtype,
                 "bias must be contiguous [N] of the output dtype");
   }
+}
+
+// fp8_scaled_mm + torch.addcmul(residual, ., gate) in the GEMM epilogue (dit.py:536-538).
+torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const torch::Tensor& mat_b,
+                                           const torch::Tensor& scales_a, const torch::Tensor& scales_b,
+                                           const torch::ScalarType& out_dtype, const c10::optional<torch::Tensor>& bias,
+                                           const torch::Tensor& residual, const torch::Tensor& gate) {
+  check_fused_gemm_operands(mat_a, mat_b, scales_a, scales_b, out_dtype, bias);
+  check_dev(residual, mat_a, "residual");
+  check_dev(gate, mat_a, "gate");
   const int64_t M = mat_a.size(0), N = mat_b.size(1);
   TORCH_CHECK(residual.is_cuda() && residual.dim() == 2 && residual.size(0) == M && residual.size(1) == N &&
                   residual.stride(1) == 1 && residual.scalar_type() == out_dtype,
@@ -439,6 +446,32 @@ torch::Tensor fp8_scaled_mm_gated_residual(const torch::Tensor& mat_a, const tor
                                            mat_a.size(1), dt_code(out_dtype), stream_of(mat_a)),
            "fp8_scaled_mm_gated_residual");
   return out;
+}
+
+// fp8_scaled_mm -> GELU-tanh -> per-token FP8 (dit.py:508-513 with the next
+// Fp8Linear's quantisation): (q [M, N] e4m3, s [M, 1] fp32); the GELU output is
+// a workspace of out_dtype.
+std::tuple<torch::Tensor, torch::Tensor> fp8_scaled_mm_gelu_quant(const torch::Tensor& mat_a,
+                                                                  const torch::Tensor& mat_b,
+                                                                  const torch::Tensor& scales_a,
+                                                                  const torch::Tensor& scales_b,
+                                                                  const torch::ScalarType& out_dtype,
+                                                                  const c10::optional<torch::Tensor>& bias) {
+  check_fused_gemm_operands(mat_a, mat_b, scales_a, scales_b, out_dtype, bias);
+  const int64_t M = mat_a.size(0), N = mat_b.size(1);
+  TORCH_CHECK(N > 0 || M == 0, "fp8_scaled_mm_gelu_quant: N must be positive");
+  const c10::cuda::CUDAGuard guard(mat_a.device());
+  torch::Tensor y = torch::empty({M, N}, mat_a.options().dtype(out_dtype));
+  torch::Tensor amax = torch::empty({M}, mat_a.options().dtype(torch::kInt32));
+  torch::Tensor q = torch::empty({M, N}, mat_a.options().dtype(torch::kFloat8_e4m3fn));
+  torch::Tensor s = torch::empty({M, 1}, mat_a.options().dtype(torch::kFloat32));
+  jo_check(jo_fp8_scaled_mm_gelu_quant(q.data_ptr(), q.stride(0), s.data_ptr<float>(), y.data_ptr(), y.stride(0),
+                                       reinterpret_cast<uint32_t*>(amax.data_ptr<int32_t>()), mat_a.data_ptr(),
+                                       mat_a.stride(0), mat_b.data_ptr(), mat_b.stride(1), scales_a.data_ptr<float>(),
+                                       scales_b.data_ptr<float>(), bias ? bias->data_ptr() : nullptr, M, N,
+                                       mat_a.size(1), dt_code(out_dtype), stream_of(mat_a)),
+           "fp8_scaled_mm_gelu_quant");
+  return {q, s};
 }
 
 
@@ -904,6 +937,9 @@ TORCH_LIBRARY(joyomni_ops, m) {
       "fp8_scaled_mm_gated_residual(Tensor mat_a, Tensor mat_b, Tensor scales_a, Tensor scales_b, "
       "ScalarType out_dtype, Tensor? bias, Tensor residual, Tensor gate) -> Tensor");
   m.def(
+      "fp8_scaled_mm_gelu_quant(Tensor mat_a, Tensor mat_b, Tensor scales_a, Tensor scales_b, "
+      "ScalarType out_dtype, Tensor? bias=None) -> (Tensor, Tensor)");
+  m.def(
       "qkv_norm_rope_pack(Tensor qkv, int num_heads, Tensor q_weight, Tensor k_weight, Tensor? cos, "
       "Tensor? sin, float eps, bool head_major, Tensor(a!)? k_pre_rope) -> (Tensor, Tensor, Tensor)");
   m.def(
@@ -950,6 +986,7 @@ TORCH_LIBRARY_IMPL(joyomni_ops, CUDA, m) {
   m.impl("sgl_per_token_quant_fp8", &sgl_per_token_quant_fp8);
   m.impl("fp8_scaled_mm", &fp8_scaled_mm);
   m.impl("fp8_scaled_mm_gated_residual", &fp8_scaled_mm_gated_residual);
+  m.impl("fp8_scaled_mm_gelu_quant", &fp8_scaled_mm_gelu_quant);
   m.impl("qkv_norm_rope_pack", &qkv_norm_rope_pack);
   m.impl("qkv_norm_rope_pack_into", &qkv_norm_rope_pack_into);
   m.impl("qkv_norm_rope_pack_host", &qkv_norm_rope_pack_host);

@@ -47,6 +47,7 @@ __all__ = [
     "timestep_mlp",
     "timestep_mlp_modulate",
     "fp8_scaled_mm_gated_residual",
+    "fp8_scaled_mm_gelu_quant",
     "rmsnorm_quant_fp8",
     "norm_scale_shift_quant_fp8",
     "qkv_norm_rope_pack_into",
@@ -187,6 +188,12 @@ def _fake_timestep_embedding(t, dim, flip_sin_to_cos, downscale_freq_shift, scal
 @torch.library.register_fake("joyomni_ops::fp8_scaled_mm_gated_residual")
 def _fake_fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate):
     return mat_a.new_empty((mat_a.shape[0], mat_b.shape[1]), dtype=out_dtype)
+
+
+@torch.library.register_fake("joyomni_ops::fp8_scaled_mm_gelu_quant")
+def _fake_fp8_scaled_mm_gelu_quant(mat_a, mat_b, scales_a, scales_b, out_dtype, bias=None):
+    m, n = mat_a.shape[0], mat_b.shape[1]
+    return mat_a.new_empty((m, n), dtype=torch.float8_e4m3fn), mat_a.new_empty((m, 1), dtype=torch.float32)
 
 
 @torch.library.register_fake("joyomni_ops::timestep_mlp")
@@ -346,6 +353,13 @@ def fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bi
     """residual + gate * fp8_scaled_mm(...) with the residual in the GEMM epilogue
     (dit.py:536-538: the down-projection and ``fused_add_gate`` in one pass)."""
     return _ops.fp8_scaled_mm_gated_residual(mat_a, mat_b, scales_a, scales_b, out_dtype, bias, residual, gate)
+
+
+def fp8_scaled_mm_gelu_quant(mat_a, mat_b, scales_a, scales_b, out_dtype, bias: Optional[torch.Tensor] = None):
+    """The MLP's fc1 -> GELU-tanh -> per-token FP8 (dit.py:508-513): (q [M, N] e4m3, s [M, 1] fp32),
+    equal to gelu_quant_fp8(fp8_scaled_mm(...)) bit for bit; GELU and the row amax run in the
+    GEMM epilogue, one more kernel quantises."""
+    return _ops.fp8_scaled_mm_gelu_quant(mat_a, mat_b, scales_a, scales_b, out_dtype, bias)
 
 
 def timestep_mlp(t, w1, b1, w2, b2, w3, b3, max_period=10000.0):

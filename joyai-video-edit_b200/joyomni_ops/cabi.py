@@ -51,6 +51,7 @@ SIGNATURES = {
     "jo_per_token_quant_fp8": [P, I64, P, P, I64, I64, I64, I32, P],
     "jo_fp8_scaled_mm": [P, I64, P, I64, P, I64, P, P, P, I64, I64, I64, I32, P],
     "jo_fp8_scaled_mm_gated_residual": [P, I64, P, I64, P, I64, P, P, P, P, I64, P, I64, I64, I64, I32, P],
+    "jo_fp8_scaled_mm_gelu_quant": [P, I64, P, P, I64, P, P, I64, P, I64, P, P, P, I64, I64, I64, I32, P],
     "jo_qkv_norm_rope_pack": [P, P, P, P, I64, I64, P, I64, I64, I64, I64, P, P, P, P, F32, P],
     "jo_gated_residual": [P, I64, P, I64, P, I64, P, I64, I64, I64, I64, I32, P],
     "jo_gated_residual_norm_scale_shift": [P, I64, P, I64, P, I64, P, I64, P, I64, I64, P, P, P, P, I64, I64,

@@ -12,7 +12,8 @@ fused sm_100a ops of this package:
                                                  split at the cache rows + attn_merge when sequence parallel
     img/txt: attn quant + out-proj GEMM          sgl_per_token_quant_fp8, fp8_scaled_mm
              gated residual + LN2 + mod + quant  gated_residual_norm_scale_shift_quant_fp8 (dit.py:525-535)
-             MLP up GEMM, GELU-tanh + quant      fp8_scaled_mm, gelu_quant_fp8   (dit.py:508-513)
+             MLP up GEMM + GELU-tanh + quant     fp8_scaled_mm_gelu_quant        (dit.py:508-513)
+               (GELU and the row amax in the GEMM epilogue, one quantisation pass)
              MLP down GEMM + gated residual      fp8_scaled_mm_gated_residual    (dit.py:536-538)
 
 Sequence parallel: the video and the text tokens of the chunk are both sharded
@@ -255,13 +256,12 @@ def _stream_out(x, attn, w: StreamWeights, m, trace=None, tag=""):
     jo.sgl_per_token_quant_fp8(attn, aq, asc)
     proj = w.proj(aq, asc)
     h, hq, hs = jo.gated_residual_norm_scale_shift_quant_fp8(x, proj, gate1, scale2, shift2, "layer", 1e-6)
-    up = w.up(hq, hs)
-    gq, gs = jo.gelu_quant_fp8(up)
+    gq, gs = jo.fp8_scaled_mm_gelu_quant(hq, w.up.wq, hs, w.up.ws, BF16, w.up.bias)
     # down projection with the gated residual in the GEMM epilogue
     out = jo.fp8_scaled_mm_gated_residual(gq, w.down.wq, gs, w.down.ws, BF16, w.down.bias, h, gate2)
     if trace is not None:
         trace.update({f"{tag}.attn": attn, f"{tag}.aq": aq, f"{tag}.as": asc, f"{tag}.proj": proj, f"{tag}.h": h,
-                      f"{tag}.hq": hq, f"{tag}.hs": hs, f"{tag}.up": up, f"{tag}.gq": gq, f"{tag}.gs": gs,
+                      f"{tag}.hq": hq, f"{tag}.hs": hs, f"{tag}.gq": gq, f"{tag}.gs": gs,
                       f"{tag}.out": out})
     return out
 

@@ -151,7 +151,12 @@ def test_block_chain(dev, hidden, heads, ffn, img_len, txt_len, cache_len):
         assert quant_matches(T[f"{tag}.aq"], T[f"{tag}.as"], T[f"{tag}.attn"])
         gemm_close(T[f"{tag}.proj"], ops.fp8_linear(T[f"{tag}.aq"], T[f"{tag}.as"], ws.proj), f"{tag} proj")
         assert_ulp_close(T[f"{tag}.h"], ops.gated_residual(x, T[f"{tag}.proj"], m[2]), 1.0, what=f"{tag} h")
-        gemm_close(T[f"{tag}.up"], ops.fp8_linear(T[f"{tag}.hq"], T[f"{tag}.hs"], ws.up), f"{tag} up")
+        # fc1 -> GELU -> FP8 (one fused op): dequantised against the oracle's GELU of its own fc1
+        g_ref = ops.gelu_tanh(ops.fp8_linear(T[f"{tag}.hq"], T[f"{tag}.hs"], ws.up)).float()
+        g_got = T[f"{tag}.gq"].float() * T[f"{tag}.gs"]
+        assert rel_err(g_got, g_ref) < 0.05, f"{tag} up + GELU + quant"
+        s_ref = g_ref.abs().amax(dim=1, keepdim=True).clamp_min(1e-8) / 448
+        assert torch.allclose(T[f"{tag}.gs"], s_ref, rtol=2e-2), f"{tag} GELU row scales"
         out_ref = ops.fp8_scaled_mm_gated_residual(T[f"{tag}.gq"], ws.down.wq, T[f"{tag}.gs"], ws.down.ws,
                                                    ws.down.bias, T[f"{tag}.h"], m[5])
         gemm_close(T[f"{tag}.out"], out_ref, f"{tag} down + gated residual")

@@ -166,3 +166,76 @@ def test_gemm_gated_residual_in_place(jo, dev):
               cabi.stream())
     torch.cuda.synchronize()
     assert_ulp_close(rg.cpu(), ref, 2.0, what="in place", atol=torch.full((M, N), 2.0 ** -10))
+
+
+# ------------------------------------------------------------------ fc1 -> GELU -> FP8
+@pytest.mark.parametrize("M,N,K,bias,dt", [(10800, 12288, 3072, True, torch.bfloat16),
+                                           (512, 12288, 3072, True, torch.bfloat16),
+                                           (100, 520, 256, False, torch.bfloat16),
+                                           (300, 264, 512, True, torch.float16),
+                                           (129, 8, 16, False, torch.bfloat16)])
+def test_gemm_gelu_quant(jo, dev, M, N, K, bias, dt):
+    """The MLP's fc1 -> GELU-tanh -> per-token FP8 in one op (GELU and the row amax in the GEMM
+    epilogue, then a quantisation pass) equals this library's unfused chain bit for bit:
+    fp8_scaled_mm, then gelu_quant_fp8.  Sizes: the BASELINE fc1 [10800, 3072] x [3072, 12288],
+    the single-CTA kernel (M <= 128), N not a multiple of the 256-column tile, fp16."""
+    aq, sa, bq, sb = operands(M, N, K, 21)
+    g = torch.Generator().manual_seed(22)
+    b = (0.1 * torch.randn(N, generator=g)).to(dt) if bias else None
+    ag, bg, sag, sbg = aq.to(dev), bq.to(dev), sa.to(dev), sb.to(dev)
+    bgpu = None if b is None else b.to(dev)
+    q, s = jo.fp8_scaled_mm_gelu_quant(ag, bg, sag, sbg, dt, bgpu)
+    up = jo.fp8_scaled_mm(ag, bg, sag, sbg, dt, bgpu)
+    q2, s2 = jo.gelu_quant_fp8(up)
+    assert torch.equal(q.view(torch.uint8), q2.view(torch.uint8)), "quantised GELU differs from the unfused chain"
+    assert torch.equal(s, s2), "row scales differ from the unfused chain"
+    # against the oracle (fc1 in float64 dot products, torch's GELU), dequantised, on sampled rows
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(23))[:64]
+    rows = torch.cat([rows, torch.tensor([0, M - 1])])
+    ref = ops.gelu_tanh(ops.fp8_scaled_mm(aq[rows], bq, sa[rows], sb, b, dt)).float()
+    got = q.cpu()[rows].float() * s.cpu()[rows]
+    rel = ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+    assert rel < 0.05, rel  # e4m3 keeps 3 mantissa bits: <= 2^-4 relative per element
+
+
+def test_gemm_gelu_quant_cabi(cabi, dev):
+    """The C ABI: guarded outputs, the GELU left in the caller's y workspace, and the amax
+    workspace reset on the stream (it starts as garbage here)."""
+    import joyomni_ops as jo
+
+    M, N, K = 260, 264, 256
+    aq, sa, bq, sb = operands(M, N, K, 24)
+    ag, bg, sag, sbg = aq.to(dev), bq.to(dev), sa.to(dev).reshape(-1), sb.to(dev).reshape(-1)
+    LDQ, LDY = N + 8, N + 16
+    qbuf, qmid = guarded_empty(M * LDQ, torch.uint8, dev)
+    sbuf, smid = guarded_empty(M, torch.float32, dev)
+    y = torch.empty(M, LDY, dtype=torch.bfloat16, device=dev)
+    amax = torch.full((M,), 0x7F7F7F7F, dtype=torch.int32, device=dev)
+    cabi.call("jo_fp8_scaled_mm_gelu_quant", qmid.data_ptr(), LDQ, smid.data_ptr(), y.data_ptr(), LDY,
+              amax.data_ptr(), ag.data_ptr(), K, bg.data_ptr(), K, sag.data_ptr(), sbg.data_ptr(), None, M, N, K,
+              cabi.JO_BF16, cabi.stream())
+    torch.cuda.synchronize()
+    assert_guard_intact(qbuf)
+    assert_guard_intact(sbuf)
+    up = jo.fp8_scaled_mm(ag, bg, sag.reshape(-1, 1), sbg.reshape(1, -1), torch.bfloat16, None)
+    gelu = jo.gelu_tanh(up)
+    assert torch.equal(y[:, :N], gelu)
+    q2, s2 = jo.gelu_quant_fp8(up)  # GELU -> FP8 of the GEMM output
+    assert torch.equal(qmid.view(M, LDQ)[:, :N], q2.view(torch.uint8))
+    assert torch.equal(smid, s2.reshape(-1))
+    assert cabi.device_fault_count() == 0
+
+
+def test_gemm_gelu_quant_rejects(cabi, dev):
+    a = torch.zeros(64, 32, dtype=FP8, device=dev)
+    w = torch.zeros(64, 32, dtype=FP8, device=dev)
+    s = torch.ones(64, device=dev)
+    q = torch.empty(64, 64, dtype=torch.uint8, device=dev)
+    y = torch.empty(64, 64, dtype=torch.bfloat16, device=dev)
+    am = torch.empty(64, dtype=torch.int32, device=dev)
+    args = lambda n, ldq, ws: (q.data_ptr(), ldq, s.data_ptr(), y.data_ptr(), 64, ws, a.data_ptr(), 32,
+                               w.data_ptr(), 32, s.data_ptr(), s.data_ptr(), None, 64, n, 32, cabi.JO_BF16, None)
+    assert cabi.status_of("jo_fp8_scaled_mm_gelu_quant", *args(0, 64, am.data_ptr())) == cabi.JO_ERR_SHAPE
+    assert cabi.status_of("jo_fp8_scaled_mm_gelu_quant", *args(64, 64, None)) == cabi.JO_ERR_INVALID
+    assert cabi.status_of("jo_fp8_scaled_mm_gelu_quant", *args(64, 68, am.data_ptr())) == cabi.JO_ERR_ALIGN
+    torch.cuda.synchronize()
