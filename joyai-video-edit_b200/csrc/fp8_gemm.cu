@@ -186,8 +186,8 @@ __device__ __forceinline__ void epi_chunk(const uint32_t* r, int n0, const GemmA
                            pack2<OutT>(o[6], o[7]));
       if constexpr (kGelu) {
         v = gelu_vec<OutT>(v);
-        amax16 = absmax_u16x2(absmax_u16x2(amax16, v.x), v.y);
-        amax16 = absmax_u16x2(absmax_u16x2(amax16, v.z), v.w);
+        amax16 = absmax16x2<OutT>(absmax16x2<OutT>(amax16, v.x), v.y);
+        amax16 = absmax16x2<OutT>(absmax16x2<OutT>(amax16, v.z), v.w);
       }
       *reinterpret_cast<uint4*>(drow + ng) = v;
     }
@@ -197,7 +197,7 @@ __device__ __forceinline__ void epi_chunk(const uint32_t* r, int n0, const GemmA
 template <int kEpi>
 __device__ __forceinline__ void epi_row_done(const GemmArgs& args, int row, bool row_ok, uint32_t amax16) {
   if constexpr ((kEpi & kEpiGelu) != 0)
-    if (row_ok) atomicMax(args.amax + row, max(amax16 & 0xffffu, amax16 >> 16));
+    if (row_ok) atomicMax(args.amax + row, amax16_bits(amax16));
 }
 
 template <typename OutT, int kEpi>

@@ -57,12 +57,33 @@ __device__ __forceinline__ float2 div2_ms(float2 x, float2 ns, float2 rc) {
 __device__ __forceinline__ uint32_t e4m3_signs(uint32_t w0, uint32_t w1) {
   return __byte_perm(w0, w1, 0x7531) & 0x80808080u;
 }
-// Running |x| maximum over packed 16-bit floats: bf16 and fp16 magnitudes
-// order exactly as their bit patterns with the sign cleared (unsigned).
-__device__ __forceinline__ uint32_t absmax_u16x2(uint32_t m, uint32_t w) {
+// Running |x| maximum over packed 16-bit floats, one instruction per word:
+// max.NaN.xorsign.abs gives max(|m|, |w|) per half with the XOR of the two
+// signs in bit 15, so the magnitude bits hold the running maximum whatever
+// sign the accumulator carries; a NaN operand makes the half NaN (as torch's
+// amax).  Typed: a bf16 pattern read as fp16 could be mistaken for a NaN.
+// amax16_bits reads the larger magnitude out of the two halves (bit patterns
+// of non-negative values order as unsigned integers).
+template <typename T>
+__device__ __forceinline__ uint32_t absmax16x2(uint32_t m, uint32_t w);
+template <>
+__device__ __forceinline__ uint32_t absmax16x2<__nv_bfloat16>(uint32_t m, uint32_t w) {
   uint32_t r;
-  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w & 0x7fff7fffu));
+  asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w));
   return r;
+}
+template <>
+__device__ __forceinline__ uint32_t absmax16x2<__half>(uint32_t m, uint32_t w) {
+  uint32_t r;
+  asm("max.NaN.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(r) : "r"(m), "r"(w));
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t absmax16x2<float>(uint32_t m, uint32_t) {
+  return m;  // not used: fp32 rows keep a float maximum
+}
+__device__ __forceinline__ uint32_t amax16_bits(uint32_t m) {
+  return max(m & 0x7fffu, (m >> 16) & 0x7fffu);
 }
 template <typename T>
 __device__ __forceinline__ float bits16_to_f(uint32_t h);

@@ -168,8 +168,8 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
   const T* bet = reinterpret_cast<const T*>(a.beta);
   const T* scr = has_mod ? reinterpret_cast<const T*>(a.scale) + row * a.mod_stride : nullptr;
   const T* shr = has_mod ? reinterpret_cast<const T*>(a.shift) + row * a.mod_stride : nullptr;
-  // |y| maximum: on the packed 16-bit patterns for bf16/fp16 (sign cleared,
-  // unsigned order = magnitude order), as floats for fp32
+  // |y| maximum: on the packed 16-bit values for bf16/fp16 (absmax16x2), as
+  // floats for fp32
   constexpr bool k16 = V == 8;
   float amax = 0.f;
   uint32_t amax16 = 0;
@@ -181,8 +181,8 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
     if constexpr (k16 && kEpi == kQuantY) {
       if (ident) {
         if (idx < nvec) {
-          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].x), raw[i].y);
-          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].z), raw[i].w);
+          amax16 = absmax16x2<T>(absmax16x2<T>(amax16, raw[i].x), raw[i].y);
+          amax16 = absmax16x2<T>(absmax16x2<T>(amax16, raw[i].z), raw[i].w);
         }
         continue;
       }
@@ -206,8 +206,8 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
       } else {
         raw[i] = Elt<T>::pack(y);  // y rounded to T, as the unfused chain materialises it
         if constexpr (k16) {
-          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].x), raw[i].y);
-          amax16 = absmax_u16x2(absmax_u16x2(amax16, raw[i].z), raw[i].w);
+          amax16 = absmax16x2<T>(absmax16x2<T>(amax16, raw[i].x), raw[i].y);
+          amax16 = absmax16x2<T>(absmax16x2<T>(amax16, raw[i].z), raw[i].w);
         } else {
           float r[V];
           Elt<T>::unpack(raw[i], r);
@@ -218,7 +218,7 @@ __device__ __forceinline__ void row_math(const RowArgs& a, int64_t row, uint4 (&
     }
   }
   if constexpr (kEpi == kQuantY) {
-    if constexpr (k16) amax = bits16_to_f<T>(max(amax16 & 0xffffu, amax16 >> 16));
+    if constexpr (k16) amax = bits16_to_f<T>(amax16_bits(amax16));
     const float s = quant_scale(row_reduce_max<kWarp>(amax, smem));
     uint8_t* qrow = a.out_q + row * a.q_stride;
     // 16-bit rows: the correctly rounded quotient from RN(1/s) (div2_ms) with the
@@ -438,10 +438,10 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
     }
     if constexpr (kEpi == kQuantY) {
       if constexpr (k16) {
-        amax16 = absmax_u16x2(amax16, raw[i].x);
-        amax16 = absmax_u16x2(amax16, raw[i].y);
-        amax16 = absmax_u16x2(amax16, raw[i].z);
-        amax16 = absmax_u16x2(amax16, raw[i].w);
+        amax16 = absmax16x2<T>(amax16, raw[i].x);
+        amax16 = absmax16x2<T>(amax16, raw[i].y);
+        amax16 = absmax16x2<T>(amax16, raw[i].z);
+        amax16 = absmax16x2<T>(amax16, raw[i].w);
       } else {
         float f[V];
         Elt<T>::unpack(raw[i], f);
@@ -453,7 +453,7 @@ __device__ __forceinline__ void row_math2(const RowArgs& a, int64_t row, uint4 (
   if constexpr (kEpi == kQuantY) {
     float amax;
     if constexpr (k16) {
-      amax = bits16_to_f<T>(red.umax(max(amax16 & 0xffffu, amax16 >> 16), 2));
+      amax = bits16_to_f<T>(red.umax(amax16_bits(amax16), 2));
     } else {
       amax = __uint_as_float(red.umax(__float_as_uint(amaxf), 2));  // |y| >= 0: bits order as values
     }

@@ -1,4 +1,4 @@
-"""Host logic of the sequence-parallel chain on CPU ranks (gloo, world_size 2).
+"""Host logic of the sequence-parallel chain on CPU ranks (gloo, world_size 2 and 4).
 
 Checks the token sharding (video and text tokens) and the in-place K/V
 all-gather placement of joyomni_ops.chain (which on GPUs runs over NCCL): every
@@ -108,6 +108,12 @@ def test_shard_range():
 def test_kv_gather_two_ranks():
     res, alive = _run("ok")
     assert not alive and res == {0: "ok", 1: "ok"}, res
+
+
+def test_kv_gather_four_ranks():
+    """Four ranks: two video tokens and one text token each, blocks in rank order."""
+    res, alive = _run("ok", world=4)
+    assert not alive and res == {r: "ok" for r in range(4)}, res
 
 
 def test_absent_rank_fails_cleanly():

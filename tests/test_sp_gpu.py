@@ -1,10 +1,10 @@
-"""Sequence-parallel chain on 2 GPUs (NCCL) against the same chain on 1 GPU.
+"""Sequence-parallel chain on 2 and 4 GPUs (NCCL) against the same chain on 1 GPU.
 
 Each rank computes its shard of the video and of the text tokens; the shards,
 concatenated, must equal the single-GPU block output (same kernels, same weights;
 attention sees the same keys, gathered in another order and split at the cache
-rows, merged by log-sum-exp).  Skipped with fewer
-than two visible GPUs.  Run with NCCL_NVLS_ENABLE=0 semantics not needed: no
+rows, merged by log-sum-exp).  Each world size is skipped with fewer visible
+GPUs than ranks.  Run with NCCL_NVLS_ENABLE=0 semantics not needed: no
 rank dies mid-collective here.
 """
 import datetime
@@ -74,29 +74,31 @@ def _worker(rank, world, port, q):
         q.put((rank, None, None, f"{type(e).__name__}: {e}\n{traceback.format_exc(limit=3)}"))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sp2_matches_single_gpu():
+@pytest.mark.parametrize("world", [2, 4])
+def test_sp_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     ref_img, ref_txt = _run_chain(torch.device("cuda", 0), 1, 0, None)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         r, a, b, err = q.get(timeout=300)
         res[r] = (a, b, err)
     for p in procs:
         p.join(60)
         if p.is_alive():
             p.kill()
-    for r in range(2):
+    for r in range(world):
         assert res[r][2] is None, res[r][2]
-    img_sp = torch.cat([res[0][0], res[1][0]])
-    txt_sp = torch.cat([res[0][1], res[1][1]])
+    img_sp = torch.cat([res[r][0] for r in range(world)])
+    txt_sp = torch.cat([res[r][1] for r in range(world)])
     for got, want in ((img_sp, ref_img), (txt_sp, ref_txt)):
         d = (got.float() - want.float()).abs().max().item()
         scale = want.float().abs().max().item()
