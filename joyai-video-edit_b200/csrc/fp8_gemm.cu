@@ -814,6 +814,11 @@ int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda,
   if ((int64_t)g.tiles_m * g.tiles_n > INT32_MAX) return fail(JO_ERR_SHAPE, "%s: too many tiles", op);
   cudaStream_t st = (cudaStream_t)stream;
   const int epi = (bias ? kEpiBias : 0) | (res ? kEpiResid : 0) | (amax ? kEpiGelu : 0);
+  if ((epi & kEpiResid) && (epi & kEpiGelu)) return fail(JO_ERR_INVALID, "%s: residual and GELU epilogues are exclusive", op);
+  // the GELU epilogue's row maxima accumulate by atomicMax: reset them once every check has passed
+  if (amax)
+    if (cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)m * sizeof(uint32_t), st))
+      return launch_failed(e, "fp8_scaled_mm_gelu_quant (amax reset)");
   switch (epi) {
     case 0: return dispatch_gemm<0>(pair, out_dtype, ma, mb, g, st, di);
     case kEpiBias: return dispatch_gemm<kEpiBias>(pair, out_dtype, ma, mb, g, st, di);
@@ -821,7 +826,7 @@ int gemm_entry(const char* op, void* d, int64_t ldd, const void* a, int64_t lda,
     case kEpiBias | kEpiResid: return dispatch_gemm<kEpiBias | kEpiResid>(pair, out_dtype, ma, mb, g, st, di);
     case kEpiGelu: return dispatch_gemm<kEpiGelu>(pair, out_dtype, ma, mb, g, st, di);
     case kEpiBias | kEpiGelu: return dispatch_gemm<kEpiBias | kEpiGelu>(pair, out_dtype, ma, mb, g, st, di);
-    default: return fail(JO_ERR_INVALID, "%s: residual and GELU epilogues are exclusive", op);
+    default: return fail(JO_ERR_INVALID, "%s: unsupported epilogue combination", op);
   }
 }
 
@@ -865,8 +870,6 @@ int jo_fp8_scaled_mm_gelu_quant(void* out_q, int64_t ldq, float* out_s, void* y,
     return fail(JO_ERR_ALIGN, "%s: out_q must be 8-byte aligned with a row stride >= N, a multiple of 8", op);
   if (reinterpret_cast<uintptr_t>(amax) & 3) return fail(JO_ERR_ALIGN, "%s: amax workspace must be 4-byte aligned", op);
   cudaStream_t st = (cudaStream_t)stream;
-  if (cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)m * sizeof(uint32_t), st))
-    return launch_failed(e, "fp8_scaled_mm_gelu_quant (amax reset)");
   if (int s = gemm_entry(op, y, ldy, a, lda, b, ldb, scale_a, scale_b, bias, nullptr, 0, nullptr, amax, m, n, k,
                          y_dtype, stream))
     return s;
