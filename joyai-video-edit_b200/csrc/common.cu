@@ -148,6 +148,19 @@ int reserve_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, con
   return JO_OK;
 }
 
+int prefer_max_carveout(const void* kernel, std::atomic<uint64_t>& done, const DeviceInfo* di, const char* what) {
+  const uint64_t bit = 1ull << di->ordinal;
+  if (done.load(std::memory_order_acquire) & bit) return JO_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                             (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(JO_ERR_CUDA, "%s: cannot set the shared-memory carveout: %s", what, cudaGetErrorString(e));
+  }
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return JO_OK;
+}
+
 int occupancy(const void* kernel, int threads, size_t smem) {
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess) {

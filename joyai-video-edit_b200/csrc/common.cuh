@@ -47,6 +47,10 @@ int symbol_address(SymbolCache& cache, const void* symbol, int dev, cudaStream_t
 // the call site) records the devices already set (bit = device ordinal).
 int reserve_smem(const void* kernel, int bytes, std::atomic<uint64_t>& done, const DeviceInfo* di,
                  const char* what);
+// Asks for `kernel` to run with the whole shared-memory carveout (once per device, as
+// reserve_smem): a kernel that shares SMs with a large-shared-memory successor then
+// leaves no carveout change (which needs the SM to drain) in that successor's way.
+int prefer_max_carveout(const void* kernel, std::atomic<uint64_t>& done, const DeviceInfo* di, const char* what);
 // Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes.
 int occupancy(const void* kernel, int threads, size_t smem);
 

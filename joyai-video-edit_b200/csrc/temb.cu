@@ -57,7 +57,49 @@ struct TembLayer {
   const __nv_bfloat16* tables;
   __nv_bfloat16* mods;
   int T;
+  // L2 prefetch of the next layer's first weight rows (null: none): rows
+  // c * pf_per + [0, pf_rows) of pf_w for c < pf_ctas, pf_row_bytes each
+  const __nv_bfloat16* pf_w;
+  int64_t pf_per;
+  int pf_rows, pf_ctas, pf_row_bytes, pf_n;
 };
+
+// Overlap of time_proj with the two small layers (measured at batch 1, graph replay of the
+// three launches: 29.3 us without any of these, 28.6 us with all three):
+//  JO_TEMB_CARVEOUT       the small layers run with the whole shared-memory carveout, so an SM
+//                         need not drain to change it before time_proj's CTAs can land there
+//  JO_TEMB_EARLY_TRIGGER  layer 2 lets time_proj launch before its own wait, so time_proj's
+//                         first weight copies go out while layer 2 finishes
+//  JO_TEMB_PF_ROWS        layer 2 prefetches into L2, after its wait, the first rows of every
+//                         time_proj CTA's block (16 rows: 14.5 MB; 32 rows measured 31.6 us,
+//                         prefetches issued before the wait 29.5 us, 4 CTAs per SM for layer 2
+//                         29.7 us)
+#ifndef JO_TEMB_PF_ROWS
+#define JO_TEMB_PF_ROWS 16
+#endif
+#ifndef JO_TEMB_PF_EARLY
+#define JO_TEMB_PF_EARLY 0
+#endif
+#ifndef JO_TEMB_EARLY_TRIGGER
+#define JO_TEMB_EARLY_TRIGGER 1
+#endif
+#ifndef JO_TEMB_CARVEOUT
+#define JO_TEMB_CARVEOUT 1
+#endif
+
+// L2 prefetch (no destination) of the next layer's first rows, one bulk prefetch per warp.
+__device__ __forceinline__ void temb_prefetch_next(const TembLayer& a) {
+  if (a.pf_w == nullptr || (threadIdx.x & 31) != 0) return;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  const int total = a.pf_ctas * a.pf_rows;
+  for (int idx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); idx < total; idx += nw) {
+    const int c = idx / a.pf_rows, j = idx - c * a.pf_rows;
+    const int64_t row = (int64_t)c * a.pf_per + j;
+    if (j >= a.pf_per || row >= a.pf_n) continue;
+    const char* src = reinterpret_cast<const char*>(a.pf_w) + row * (int64_t)a.pf_row_bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(a.pf_row_bytes) : "memory");
+  }
+}
 
 struct TembCfg {
   int rows_per_unit;    // consecutive weight rows per bulk copy
@@ -213,7 +255,11 @@ constexpr int kDirectWarps = 8;
 constexpr int kDirectMaxB = 2;
 
 template <int kB, int kV, bool kSinIn, bool kSilu, bool kEarly>
-__global__ void __launch_bounds__(kDirectWarps * 32) temb_direct_kernel(const TembLayer a, int b0) {
+#ifndef JO_TEMB_DIRECT_MINB
+#define JO_TEMB_DIRECT_MINB 1
+#endif
+__global__ void __launch_bounds__(kDirectWarps * 32, JO_TEMB_DIRECT_MINB)
+    temb_direct_kernel(const TembLayer a, int b0) {
   __shared__ __align__(16) __nv_bfloat16 xs[kB * kV * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = a.K;
@@ -227,10 +273,18 @@ __global__ void __launch_bounds__(kDirectWarps * 32) temb_direct_kernel(const Te
       w[j] = (row_ok && kk < K) ? ld_stream(a.w + n * K + kk) : make_uint4(0, 0, 0, 0);
     }
   };
-  if constexpr (kEarly) load_w();
+  if constexpr (kEarly) {
+    load_w();
+    // Layer 2 was launched only once layer 1 had passed its own wait (every kernel
+    // before the MLP has completed), so time_proj may start its weight copies now;
+    // it reads its input only after its own wait (this layer complete).
+    if (JO_TEMB_EARLY_TRIGGER) pdl_trigger();
+    if (JO_TEMB_PF_EARLY) temb_prefetch_next(a);
+  }
   pdl_wait();  // the previous layer's output (our input) is complete from here on
   pdl_trigger();
   if constexpr (!kEarly) load_w();
+  if (!JO_TEMB_PF_EARLY) temb_prefetch_next(a);
   if constexpr (kSinIn) {  // the sinusoid, with the staged kernel's arithmetic
     const int half = K / 2;
     for (int idx = threadIdx.x; idx < kB * half; idx += blockDim.x) {
@@ -291,8 +345,14 @@ __global__ void __launch_bounds__(kDirectWarps * 32) temb_direct_kernel(const Te
 }
 
 template <int kB, int kV, bool kSinIn, bool kSilu>
-int launch_direct(const TembLayer& a, int b0, cudaStream_t st) {
+int launch_direct(const TembLayer& a, int b0, cudaStream_t st, const DeviceInfo* di) {
   const int64_t grid = cdiv(a.N, kDirectWarps);
+  if (JO_TEMB_CARVEOUT) {
+    static std::atomic<uint64_t> carved{0};  // one per kernel instantiation
+    if (int s = prefer_max_carveout((const void*)temb_direct_kernel<kB, kV, kSinIn, kSilu, !kSinIn>, carved, di,
+                                    "timestep_mlp"))
+      return s;
+  }
   if (cudaError_t e = launch_pdl(temb_direct_kernel<kB, kV, kSinIn, kSilu, !kSinIn>, dim3((unsigned)grid),
                                  dim3(kDirectWarps * 32), 0, st, a, b0))
     return launch_failed(e, "timestep_mlp");
@@ -303,20 +363,20 @@ int launch_direct(const TembLayer& a, int b0, cudaStream_t st) {
 // chunks of at most kDirectMaxB rows): returns true when it took the layer.
 constexpr int64_t kDirectBytes = 32ll << 20;
 template <bool kSinIn, bool kSilu>
-bool try_direct(const TembLayer& a, cudaStream_t st, int& status) {
+bool try_direct(const TembLayer& a, cudaStream_t st, const DeviceInfo* di, int& status) {
   if ((int64_t)a.N * a.K * 2 > kDirectBytes || a.K > kMaxK) return false;
   status = JO_OK;
   for (int b0 = 0; b0 < a.B && status == JO_OK; b0 += kDirectMaxB) {  // one launch at the model's batch
     const bool one = a.B - b0 == 1;
     const int kv = (a.K + 255) / 256;
     if (kv <= 1)
-      status = one ? launch_direct<1, 1, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 1, kSinIn, kSilu>(a, b0, st);
+      status = one ? launch_direct<1, 1, kSinIn, kSilu>(a, b0, st, di) : launch_direct<2, 1, kSinIn, kSilu>(a, b0, st, di);
     else if (kv <= 4)
-      status = one ? launch_direct<1, 4, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 4, kSinIn, kSilu>(a, b0, st);
+      status = one ? launch_direct<1, 4, kSinIn, kSilu>(a, b0, st, di) : launch_direct<2, 4, kSinIn, kSilu>(a, b0, st, di);
     else if (kv <= 12)
-      status = one ? launch_direct<1, 12, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 12, kSinIn, kSilu>(a, b0, st);
+      status = one ? launch_direct<1, 12, kSinIn, kSilu>(a, b0, st, di) : launch_direct<2, 12, kSinIn, kSilu>(a, b0, st, di);
     else
-      status = one ? launch_direct<1, 16, kSinIn, kSilu>(a, b0, st) : launch_direct<2, 16, kSinIn, kSilu>(a, b0, st);
+      status = one ? launch_direct<1, 16, kSinIn, kSilu>(a, b0, st, di) : launch_direct<2, 16, kSinIn, kSilu>(a, b0, st, di);
   }
   return true;
 }
@@ -337,7 +397,7 @@ int launch_layer(const TembLayer& a, cudaStream_t st, const DeviceInfo* di) {
   // the time_proj layer (ModulateWan tables in its epilogue) always streams
   if (kSilu && a.B <= kDirectMaxB) {
     int s = JO_OK;
-    if (try_direct<kSinIn, kSilu>(a, st, s)) return s;
+    if (try_direct<kSinIn, kSilu>(a, st, di, s)) return s;
   }
   for (int b0 = 0; b0 < a.B; b0 += kMaxB) {
     const int nb = std::min(kMaxB, a.B - b0);
@@ -399,7 +459,18 @@ int timestep_mlp_run(void* vec, const float* t, int64_t batch, const void* w1, c
   l.y = s2;
   l.K = (int)dim;
   l.N = (int)dim;
+  if (JO_TEMB_PF_ROWS > 0) {  // time_proj's partition: one CTA per SM, 1 row per unit at dim >= 3072
+    const int64_t r3 = std::max<int64_t>(1, 6144 / (dim * 2));
+    const int64_t g3 = std::max<int64_t>(1, std::min<int64_t>(di->sm_count, cdiv(proj_dim, r3)));
+    l.pf_w = reinterpret_cast<const __nv_bfloat16*>(w3);
+    l.pf_per = cdiv(proj_dim, g3);
+    l.pf_rows = JO_TEMB_PF_ROWS;
+    l.pf_ctas = (int)g3;
+    l.pf_row_bytes = (int)(dim * 2);
+    l.pf_n = (int)proj_dim;
+  }
   if (int s = launch_layer<false, true>(l, st, di)) return s;
+  l.pf_w = nullptr;
   // layer 3: time_proj
   l.x = s2;
   l.w = reinterpret_cast<const __nv_bfloat16*>(w3);
