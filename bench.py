@@ -438,6 +438,7 @@ class Chain(Workload):
         self.shape = {"hidden": self.D, "heads": self.H, "ffn": self.F, "img_tokens": self.L, "txt_tokens": self.T,
                       "cache_tokens": self.CACHE, "weights": "random init N(0,0.02), FP8 per-channel"}
         self.world, self.rank, self.group = 1, 0, None
+        self.gather = "ce"  # K/V gather at P > 1: "ce" (copy engines, chain.PeerGather) or "nccl"
 
     def flops(self):
         D, F, L, T = self.D, self.F, self.L, self.T
@@ -461,18 +462,20 @@ class Chain(Workload):
         cos, sin = rope.video_chunk_tables(3, 45, 80, 7, dims=(44, 42, 42))
         b0, b1 = chain.shard_range(self.L, self.world, self.rank)
         cos, sin = cos[b0:b1].to(dev), sin[b0:b1].to(dev)
-        bufs = chain.KVBuffers(self.CACHE, self.L, self.T, self.H, self.D // self.H, self.world, dev)
+        ce = self.group is not None and self.gather == "ce"
+        bufs = chain.KVBuffers(self.CACHE, self.L, self.T, self.H, self.D // self.H, self.world, dev, ipc=ce)
         bufs.k.normal_()
         bufs.v.normal_()
         side = torch.cuda.Stream()
-        st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side)
+        peers = chain.PeerGather(bufs, self.rank, self.world, self.group) if ce else None
+        st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side, peers=peers)
         out = self.step(st)
         return dict(st, inputs={"img": img, "txt": txt}, outputs={"img_out": out[0], "txt_out": out[1]})
 
     def step(self, st):
         return st["chain"].block_forward(st["img"], st["txt"], st["vec"], st["cos"], st["sin"], st["w"], st["bufs"],
                                          group=self.group, rank=self.rank, side_stream=st["side"],
-                                         events=st.get("events"))
+                                         events=st.get("events"), peers=st.get("peers"))
 
     def e2e_step(self, st, host_in, host_out):
         st["img"].copy_(host_in["img"], non_blocking=True)
@@ -692,23 +695,32 @@ def time_graph(graph, world: int) -> float:
 def time_allgather(wl, st, world: int, rank: int, iters: int = 10) -> dict:
     """The chain's K/V all-gather alone (the chunk's K and V rows, in place), every rank
     taking part; CUDA events on the launching stream, max over ranks."""
-    bufs, chain = st["bufs"], st["chain"]
+    bufs, chain, peers = st["bufs"], st["chain"], st.get("peers")
+
+    def gather():
+        if peers is not None:
+            peers.gather(torch.cuda.current_stream())
+        else:
+            chain.gather_chunk_kv(bufs, rank, wl.group)
+
     for _ in range(2):
-        chain.gather_chunk_kv(bufs, rank, wl.group)
+        gather()
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(iters):
-        chain.gather_chunk_kv(bufs, rank, wl.group)
+        gather()
     e1.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / iters, world)
     total = 2 * (wl.L + wl.T) * wl.D * 2  # K and V rows of the chunk (video + text), bf16
     return {"us": round(ms * 1e3, 1), "bytes_received_per_rank": int(total * (world - 1) / world),
             "bus_gbs": round(total * (world - 1) / world / (ms * 1e-3) / 1e9, 1),
-            "note": "in-place all_gather_into_tensor of the chunk's K and V rows of every rank (NCCL), alone; "
-                    "in the block it runs on a side stream beside the attention over the cache rows"}
+            "method": "copy engines (CUDA IPC peer pulls, chain.PeerGather)" if peers is not None else
+                      "NCCL all_gather_into_tensor, in place",
+            "note": "the chunk's K and V rows of every rank gathered alone; in the block the gather runs on a "
+                    "side stream beside the attention over the cache rows"}
 
 
 def cpu_baseline(wl: Workload, min_seconds: float = 10.0):
@@ -913,6 +925,7 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
     wl = workloads()["chain"]
     wl.world, wl.rank = world, rank
     wl.group = dist.group.WORLD if world > 1 else None
+    wl.gather = args.gather
     st = wl.make(dev, seed=1)
     for _ in range(max(args.warmup, 3)):
         wl.step(st)
@@ -920,9 +933,10 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
     steps = max(5, args.steps // 2)
     total_ms, per_ms = time_device(lambda i: wl.step(st), steps, world)
     ms = max_over_ranks(total_ms / steps, world)
+    how = "copy-engine peer pulls (CUDA IPC)" if wl.gather == "ce" else "one NCCL all-gather per tensor"
     rec = {"config": {**wl.config(), "parallelism": f"sequence parallel over {world} GPU(s): video and text "
-                                                   f"tokens sharded, one NCCL all-gather of the chunk K/V per "
-                                                   f"tensor, overlapped with the attention over the cache rows"},
+                                                   f"tokens sharded, the chunk K/V gathered by {how}, "
+                                                   f"overlapped with the attention over the cache rows"},
            "us_per_block": round(ms * 1e3, 1), "steps": steps,
            "tflops": round(wl.flops() / (ms * 1e-3) / 1e12, 1),
            "timing": "eager steps (NCCL collective and library attention inside), CUDA events, max over ranks"}
@@ -937,9 +951,22 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
             exposed.append(max(0.0, ev["overlap_end"].elapsed_time(ev["gather_end"])))
         st.pop("events")
         ex = max_over_ranks(statistics.median(exposed), world)
+        if st.get("peers") is not None:  # every rank learns whether any rank's bounded wait expired
+            import torch.distributed as dist
+
+            from joyomni_ops import cabi
+
+            f = torch.tensor([float(cabi.device_fault_count())], device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.MAX)
+            if f.item() > 0:
+                rec["error"] = ("a bounded wait of the copy-engine K/V gather expired on some rank: "
+                                "the chain timings above are not valid")
         g_us = rec["allgather"]["us"]
         rec["allgather"].update(exposed_us=round(ex * 1e3, 1),
                                 hidden_frac=round(max(0.0, 1 - ex * 1e3 / g_us), 3) if g_us > 0 else None)
+    if st.get("peers") is not None:
+        st["peers"].close()
+        st["bufs"].close()
     del st
     torch.cuda.empty_cache()
     if world == 1 and not args.no_cpu_baseline:
@@ -991,6 +1018,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--no-per-op", action="store_true", help="skip the per-op records")
     ap.add_argument("--no-chain", action="store_true", help="skip the per-block chain record")
+    ap.add_argument("--gather", choices=["ce", "nccl"], default="ce",
+                    help="the chain's K/V all-gather at N > 1: copy engines (CUDA IPC) or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -4,7 +4,8 @@
  * Every entry point takes plain device pointers, element counts, element
  * strides (in elements, not bytes), a dtype code and a cudaStream_t passed as
  * `void*`, and returns an int status (JO_OK == 0, negative on error).  Nothing
- * here allocates device memory; outputs are caller-owned.  No C++ exception
+ * here allocates device memory but jo_ipc_alloc (the IPC-shareable buffers of
+ * the copy-engine K/V gather); outputs are caller-owned.  No C++ exception
  * crosses this boundary; jo_last_error() returns the message of the last
  * failing call made on the calling host thread.
  *
@@ -363,6 +364,39 @@ JO_API int jo_gated_residual_norm_scale_shift_quant_fp8(
     const void* beta, const void* scale, const void* shift, int64_t mod_rows,
     int64_t mod_row_stride, int64_t rows, int64_t cols, int norm, int dtype, float eps,
     void* stream);
+
+/* ---- copy-engine K/V all-gather between the ranks of one node --------- *
+ * Replaces the NCCL all_gather_into_tensor of the chunk's K/V at the attention
+ * boundary of the sequence-parallel block (deploy/xvideo/models/dit/dit.py:
+ * 154-189, 498; one process per GPU): every rank maps the other ranks' K/V
+ * buffers over CUDA IPC and pulls their blocks with the copy engines over
+ * NVLink, so no SM is taken from the attention that the gather overlaps.  The
+ * host side (joyomni_ops.chain) orders the steps with two flag words per peer. */
+#define JO_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc of `bytes` (a whole allocation, as IPC export requires), zeroed
+ * (synchronously); jo_ipc_free releases it. */
+JO_API int jo_ipc_alloc(int64_t bytes, void** ptr);
+JO_API int jo_ipc_free(void* ptr);
+/* The IPC handle (JO_IPC_HANDLE_BYTES bytes) of an allocation made by
+ * jo_ipc_alloc, for another process on the node to open. */
+JO_API int jo_ipc_handle(const void* ptr, void* handle);
+/* Maps another process's allocation into the current device's context with
+ * peer access (cudaIpcMemLazyEnablePeerAccess); jo_ipc_close unmaps it. */
+JO_API int jo_ipc_open(const void* handle, void** ptr);
+JO_API int jo_ipc_close(void* ptr);
+/* One kernel on `stream`: after a system-wide fence, stores `value` with
+ * release semantics into each non-null 8-byte word peer_flags[q], q < world
+ * (<= 16): this rank's flag word in each peer's (mapped) flag array. */
+JO_API int jo_peer_signal(void* const* peer_flags, int world, uint64_t value, void* stream);
+/* One kernel on `stream`: waits until flags[q] >= value (acquire loads) for
+ * every q < world other than `skip`.  Bounded: after 2 s without progress the
+ * device fault counter (jo_device_fault_count) is raised and the kernel
+ * returns, so a rank that never signals ends in a recorded fault. */
+JO_API int jo_peer_wait(const uint64_t* flags, int world, int skip, uint64_t value, void* stream);
+/* cudaMemcpyAsync of `bytes` device bytes on `stream` (a peer's mapped memory
+ * as the source: a copy-engine transfer over NVLink). */
+JO_API int jo_peer_copy(void* dst, const void* src, int64_t bytes, void* stream);
 
 #ifdef __cplusplus
 }

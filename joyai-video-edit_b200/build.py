@@ -37,7 +37,7 @@ NVCC_FLAGS = ARCH + [
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
 CU_SOURCES = ["common.cu", "rows.cu", "rows_bf16.cu", "rows_f16.cu", "rows_f32.cu", "qkv.cu", "elementwise.cu",
-              "fp8_gemm.cu", "temb.cu", "host_io.cu", "attn.cu"]
+              "fp8_gemm.cu", "temb.cu", "host_io.cu", "attn.cu", "peer.cu"]
 LIB = OUT / "libjoyomni_b200.so"
 SHIM = OUT / "_C.so"
 

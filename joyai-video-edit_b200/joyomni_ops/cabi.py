@@ -33,7 +33,9 @@ class JoView4(C.Structure):
 P = C.c_void_p
 I64 = C.c_int64
 I32 = C.c_int
+U64 = C.c_uint64
 F32 = C.c_float
+PP = C.POINTER(C.c_void_p)
 FP = C.POINTER(C.c_float)
 
 # name -> argtypes (restype is int unless listed in _RESTYPES)
@@ -69,7 +71,16 @@ SIGNATURES = {
     "jo_gelu_quant_fp8": [P, I64, P, P, I64, I64, I64, I32, P],
     "jo_gated_residual_norm_scale_shift_quant_fp8": [P, I64, P, I64, P, P, I64, P, I64, P, I64, I64, P, P, P, P,
                                                      I64, I64, I64, I64, I32, I32, F32, P],
+    "jo_ipc_alloc": [I64, PP],
+    "jo_ipc_free": [P],
+    "jo_ipc_handle": [P, P],
+    "jo_ipc_open": [P, PP],
+    "jo_ipc_close": [P],
+    "jo_peer_signal": [P, I32, U64, P],
+    "jo_peer_wait": [P, I32, I32, U64, P],
+    "jo_peer_copy": [P, P, I64, P],
 }
+JO_IPC_HANDLE_BYTES = 64
 _RESTYPES = {"jo_status_name": C.c_char_p, "jo_last_error": C.c_char_p, "jo_launch_count": C.c_uint64}
 
 _lib = None

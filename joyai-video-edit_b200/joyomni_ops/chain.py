@@ -144,7 +144,7 @@ class KVBuffers:
     """
 
     def __init__(self, cache_len: int, img_len: int, txt_len: int, heads: int, head_dim: int, world: int,
-                 device, dtype=BF16, store: bool = False):
+                 device, dtype=BF16, store: bool = False, ipc: bool = False):
         self.cache_len, self.img_len, self.txt_len = cache_len, img_len, txt_len
         if img_len % world or txt_len % world:
             raise ValueError(f"{img_len} video / {txt_len} text tokens do not split evenly over {world} ranks")
@@ -152,8 +152,14 @@ class KVBuffers:
         self.txt_local = txt_len // world
         self.block = self.local + self.txt_local
         s_kv = cache_len + img_len + txt_len
-        self.k = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
-        self.v = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
+        self.row_bytes = heads * head_dim * torch.tensor([], dtype=dtype).element_size()
+        self._ipc = []
+        if ipc:  # whole allocations that the other ranks can map (the copy-engine gather)
+            self._ipc = [IpcAlloc(s_kv * self.row_bytes, device) for _ in range(2)]
+            self.k, self.v = (a.tensor((s_kv, heads, head_dim), dtype) for a in self._ipc)
+        else:
+            self.k = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
+            self.v = torch.empty(s_kv, heads, head_dim, dtype=dtype, device=device)
         self.q = torch.empty(self.block, heads, head_dim, dtype=dtype, device=device)
         self.slots = cache_len // img_len
         self.k_pre = self.v_stage = None
@@ -164,6 +170,14 @@ class KVBuffers:
             self.v_stage = torch.empty(img_len, heads, head_dim, dtype=dtype, device=device)
         self.k_pre_of = list(range(self.slots))
         self.spare = self.slots
+
+    def close(self) -> None:
+        """Frees IPC-allocated K/V buffers (after every peer has unmapped them:
+        ``PeerGather.close`` first)."""
+        self.k = self.v = None
+        for a in self._ipc:
+            a.free()
+        self._ipc = []
 
     def cache_slot_rows(self, slot: int):
         return slice(slot * self.img_len, (slot + 1) * self.img_len)
@@ -183,6 +197,143 @@ class KVBuffers:
     def gathered_rows(self):
         """Every rank's block (all rows after the cache)."""
         return slice(self.cache_len, self.cache_len + self.img_len + self.txt_len)
+
+
+class IpcAlloc:
+    """A whole device allocation of ``nbytes`` (``jo_ipc_alloc``, zeroed) on ``device``, which
+    other processes on the node can map (``jo_ipc_handle`` / ``jo_ipc_open``).  ``tensor``
+    views it; ``free`` releases it (no view may be used afterwards)."""
+
+    def __init__(self, nbytes: int, device):
+        import ctypes as C
+
+        from joyomni_ops import cabi
+
+        self.device = torch.device(device)
+        with torch.cuda.device(self.device):
+            p = C.c_void_p()
+            cabi.call("jo_ipc_alloc", nbytes, C.byref(p))
+        self.ptr, self.nbytes = p.value, nbytes
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (self.ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+    def tensor(self, shape, dtype) -> torch.Tensor:
+        return torch.as_tensor(self, device=self.device).view(dtype).view(shape)
+
+    def handle(self) -> bytes:
+        import ctypes as C
+
+        from joyomni_ops import cabi
+
+        h = C.create_string_buffer(cabi.JO_IPC_HANDLE_BYTES)
+        cabi.call("jo_ipc_handle", self.ptr, h)
+        return h.raw
+
+    def free(self) -> None:
+        from joyomni_ops import cabi
+
+        if self.ptr is not None:
+            with torch.cuda.device(self.device):
+                cabi.call("jo_ipc_free", self.ptr)
+            self.ptr = None
+
+
+class PeerGather:
+    """Copy-engine all-gather of the chunk's K/V blocks over the ranks of ``group`` (one
+    process per GPU of one node), in place of the NCCL ``all_gather_into_tensor`` of
+    ``gather_chunk_kv``: every rank maps the other ranks' K/V buffers (``KVBuffers(...,
+    ipc=True)``, CUDA IPC) and pulls each peer's block with one copy-engine transfer per
+    (peer, tensor), on a stream of its own, so the gather takes no SMs from the attention
+    over the cache rows that it overlaps.
+
+    Ordering (two 8-byte flag words per peer in each rank's IPC-mapped flag array):
+    ``gather`` (step e) stores e into ready[r] on every peer once this rank's block is
+    written, waits until every peer's ready word on this rank reaches e, pulls, then stores
+    e into done[r] on every peer; ``before_write`` (on the compute stream, before the rank's
+    pack overwrites its block for step e + 1) waits until every peer's done word reaches e.
+    Every wait is a bounded kernel (2 s, then the device fault counter is raised)."""
+
+    def __init__(self, bufs: KVBuffers, rank: int, world: int, group):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        from joyomni_ops import cabi
+
+        if not bufs._ipc:
+            raise ValueError("PeerGather needs KVBuffers(..., ipc=True)")
+        self.bufs, self.rank, self.world, self.group = bufs, rank, world, group
+        dev = bufs.k.device
+        self._flags = IpcAlloc(max(256, 16 * world), dev)  # ready[world] | done[world], zeroed
+        mine = [bufs._ipc[0].handle(), bufs._ipc[1].handle(), self._flags.handle()]
+        every = [None] * world
+        dist.all_gather_object(every, mine, group=group)
+        self._mapped = []
+        self.peer_k, self.peer_v = {}, {}
+        self._ready_tab = (C.c_void_p * world)()
+        self._done_tab = (C.c_void_p * world)()
+        with torch.cuda.device(dev):
+            for q in range(world):
+                if q == rank:
+                    continue
+                ptrs = []
+                for h in every[q]:
+                    p = C.c_void_p()
+                    cabi.call("jo_ipc_open", C.create_string_buffer(h, len(h)), C.byref(p))
+                    ptrs.append(p.value)
+                    self._mapped.append(p.value)
+                self.peer_k[q], self.peer_v[q] = ptrs[0], ptrs[1]
+                self._ready_tab[q] = ptrs[2] + 8 * rank
+                self._done_tab[q] = ptrs[2] + 8 * (world + rank)
+        self._local_ready = self._flags.ptr
+        self._local_done = self._flags.ptr + 8 * world
+        self.step = 0
+        self._streams = {(q, t): torch.cuda.Stream(dev) for q in self.peer_k for t in range(2)}
+        dist.barrier(group=group)
+
+    def before_write(self, stream: torch.cuda.Stream) -> None:
+        """On ``stream``, before this rank's pack rewrites its block: every peer has pulled
+        the previous step's block."""
+        from joyomni_ops import cabi
+
+        if self.step > 0:
+            cabi.call("jo_peer_wait", self._local_done, self.world, self.rank, self.step, stream.cuda_stream)
+
+    def gather(self, stream: torch.cuda.Stream) -> None:
+        """On ``stream`` (after this rank's block is written): publish the block, wait for
+        every peer's, pull them all; ``stream`` then orders after every pull."""
+        from joyomni_ops import cabi
+
+        self.step += 1
+        s = stream.cuda_stream
+        cabi.call("jo_peer_signal", self._ready_tab, self.world, self.step, s)
+        cabi.call("jo_peer_wait", self._local_ready, self.world, self.rank, self.step, s)
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        b = self.bufs
+        n = b.block * b.row_bytes
+        for (q, t), cs in self._streams.items():
+            cs.wait_event(ready)
+            off = b.block_rows(q).start * b.row_bytes
+            dst, src = (b.k, self.peer_k[q]) if t == 0 else (b.v, self.peer_v[q])
+            cabi.call("jo_peer_copy", dst.data_ptr() + off, src + off, n, cs.cuda_stream)
+            stream.wait_stream(cs)
+        cabi.call("jo_peer_signal", self._done_tab, self.world, self.step, s)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees the flag array; every rank calls it (it
+        ends with a barrier, after which ``bufs.close()`` may free the K/V buffers)."""
+        import torch.distributed as dist
+
+        from joyomni_ops import cabi
+
+        torch.cuda.synchronize()
+        with torch.cuda.device(self._flags.device):
+            for p in self._mapped:
+                cabi.call("jo_ipc_close", p)
+        self._mapped = []
+        dist.barrier(group=self.group)
+        self._flags.free()
 
 
 def store_chunk_kv(bufs: KVBuffers, rank: int, group) -> None:
@@ -306,7 +457,7 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
                   w: BlockWeights, bufs: KVBuffers, group=None, rank: int = 0,
                   side_stream: Optional[torch.cuda.Stream] = None, trace: Optional[dict] = None,
                   events: Optional[dict] = None, mods: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                  store: bool = False):
+                  store: bool = False, peers: Optional[PeerGather] = None):
     """One double-stream block for one chunk.
 
     img: bf16 [L_local, D] (this rank's video tokens), txt: bf16 [T_local, D] (this rank's
@@ -323,6 +474,8 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
     ``store``: a store forward (buffers made with ``store=True``): the image pack also
     writes this rank's pre-RoPE keys into the spare ``k_pre`` slot; ``store_chunk_kv``
     then replicates the chunk.
+    ``peers`` (with ``group``): gather the chunk's K/V with the copy engines
+    (``PeerGather``) instead of the NCCL all-gather.
     """
     H = w.heads
     L = img.shape[0]
@@ -332,6 +485,8 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
         mi = modulation(w.img.mod_table, vec)
         mt = modulation(w.txt.mod_table, vec)
     k_pre = bufs.k_pre[bufs.spare][rank * bufs.local:(rank + 1) * bufs.local] if store else None
+    if group is not None and peers is not None:
+        peers.before_write(torch.cuda.current_stream())
     _stream_qkv(img, w.img, mi, H, cos, sin, bufs.q[:L], bufs.k[bufs.img_kv_rows(rank)],
                 bufs.v[bufs.img_kv_rows(rank)], trace, "img", k_pre)
     _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows(rank)],
@@ -345,7 +500,10 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
         with torch.cuda.stream(side):
             if events is not None:
                 events["gather_start"] = _event(side)
-            gather_chunk_kv(bufs, rank, group)
+            if peers is not None:
+                peers.gather(side)
+            else:
+                gather_chunk_kv(bufs, rank, group)
             if events is not None:
                 events["gather_end"] = _event(side)
         gathered = side

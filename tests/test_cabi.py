@@ -161,7 +161,8 @@ def header_params():
 def ctype_kind(c_type):
     if c_type.endswith("*"):
         return "ptr"
-    return {"int64_t": "i64", "int": "i32", "float": "f32", "jo_view4": "view4", "uint32_t": "u32"}[c_type]
+    return {"int64_t": "i64", "int": "i32", "float": "f32", "jo_view4": "view4", "uint32_t": "u32",
+            "uint64_t": "u64"}[c_type]
 
 
 def test_ctypes_argument_kinds_match_header(cabi):
@@ -169,7 +170,7 @@ def test_ctypes_argument_kinds_match_header(cabi):
     import ctypes as C
 
     kind = {C.c_void_p: "ptr", C.c_int64: "i64", C.c_int32: "i32", C.c_int: "i32", C.c_float: "f32",
-            cabi.JoView4: "view4"}
+            C.c_uint64: "u64", cabi.JoView4: "view4"}
     decls = header_params()
     assert set(decls) == set(cabi.SIGNATURES)
     for name, c_params in decls.items():
