@@ -161,3 +161,34 @@ def test_block_with_peer_gather_matches_single_gpu(world):
             assert d <= 1e-2 * scale, f"step {step}: differs from single GPU by {d} (max |ref| {scale})"
     for r in range(world):  # the second step repeats the first bit for bit
         assert torch.equal(res[r][0][0][0], res[r][0][1][0]) and torch.equal(res[r][0][0][1], res[r][0][1][1])
+
+
+def test_peer_flags_one_gpu(dev):
+    """The flag kernels on one GPU with this process's own flag array: a signalled word
+    releases the wait at once; a word that nothing sets makes the bounded wait expire
+    (2 s): the fault counter records it and the device stays usable."""
+    import ctypes as C
+    import time
+
+    from joyomni_ops import cabi, chain
+
+    cabi.device_fault_count()  # clear
+    flags = chain.IpcAlloc(256, dev)
+    try:
+        world = 4
+        tab = (C.c_void_p * world)(*[flags.ptr + 8 * q for q in range(world)])
+        st = torch.cuda.current_stream().cuda_stream
+        cabi.call("jo_peer_signal", tab, world, 7, st)
+        cabi.call("jo_peer_wait", flags.ptr, world, 0, 7, st)
+        torch.cuda.synchronize()
+        assert cabi.device_fault_count() == 0
+        assert flags.tensor((32,), torch.int64)[:world].tolist() == [7] * world
+        t0 = time.perf_counter()
+        cabi.call("jo_peer_wait", flags.ptr, world, 0, 8, st)  # nothing stores 8
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 >= 1.5
+        assert cabi.device_fault_count() == world - 1  # one expiry per waited word (q != skip)
+        x = torch.ones(4, device=dev)
+        assert (x + 1).sum().item() == 8  # the context is still usable
+    finally:
+        flags.free()
