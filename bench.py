@@ -467,8 +467,14 @@ class Chain(Workload):
         bufs.k.normal_()
         bufs.v.normal_()
         side = torch.cuda.Stream()
-        peers = chain.PeerGather(bufs, self.rank, self.world, self.group) if ce else None
-        st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side, peers=peers)
+        peers, note = None, None
+        if ce:
+            try:  # raises on every rank together when any rank cannot map its peers
+                peers = chain.PeerGather(bufs, self.rank, self.world, self.group)
+            except RuntimeError as e:
+                note = f"{e}; the chunk K/V gathered by NCCL instead"
+        st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side, peers=peers,
+                  gather_note=note)
         out = self.step(st)
         return dict(st, inputs={"img": img, "txt": txt}, outputs={"img_out": out[0], "txt_out": out[1]})
 
@@ -933,13 +939,16 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
     steps = max(5, args.steps // 2)
     total_ms, per_ms = time_device(lambda i: wl.step(st), steps, world)
     ms = max_over_ranks(total_ms / steps, world)
-    how = "copy-engine peer pulls (CUDA IPC)" if wl.gather == "ce" else "one NCCL all-gather per tensor"
-    rec = {"config": {**wl.config(), "parallelism": f"sequence parallel over {world} GPU(s): video and text "
-                                                   f"tokens sharded, the chunk K/V gathered by {how}, "
-                                                   f"overlapped with the attention over the cache rows"},
+    how = "copy-engine peer pulls (CUDA IPC)" if st.get("peers") is not None else "one NCCL all-gather per tensor"
+    par = ("one GPU: every token local, no K/V gather" if world == 1 else
+           f"sequence parallel over {world} GPUs: video and text tokens sharded, the chunk K/V gathered by "
+           f"{how}, overlapped with the attention over the cache rows")
+    rec = {"config": {**wl.config(), "parallelism": par},
            "us_per_block": round(ms * 1e3, 1), "steps": steps,
            "tflops": round(wl.flops() / (ms * 1e-3) / 1e12, 1),
            "timing": "eager steps (NCCL collective and library attention inside), CUDA events, max over ranks"}
+    if st.get("gather_note"):
+        rec["gather_note"] = st["gather_note"]
     if world > 1:
         rec["allgather"] = time_allgather(wl, st, world, rank)
         exposed = []
@@ -966,7 +975,7 @@ def run_chain(args, world: int, rank: int, dev) -> dict:
                                 hidden_frac=round(max(0.0, 1 - ex * 1e3 / g_us), 3) if g_us > 0 else None)
     if st.get("peers") is not None:
         st["peers"].close()
-        st["bufs"].close()
+    st["bufs"].close()
     del st
     torch.cuda.empty_cache()
     if world == 1 and not args.no_cpu_baseline:

@@ -272,19 +272,34 @@ class PeerGather:
         self.peer_k, self.peer_v = {}, {}
         self._ready_tab = (C.c_void_p * world)()
         self._done_tab = (C.c_void_p * world)()
+        err = None
         with torch.cuda.device(dev):
-            for q in range(world):
-                if q == rank:
-                    continue
-                ptrs = []
-                for h in every[q]:
-                    p = C.c_void_p()
-                    cabi.call("jo_ipc_open", C.create_string_buffer(h, len(h)), C.byref(p))
-                    ptrs.append(p.value)
-                    self._mapped.append(p.value)
-                self.peer_k[q], self.peer_v[q] = ptrs[0], ptrs[1]
-                self._ready_tab[q] = ptrs[2] + 8 * rank
-                self._done_tab[q] = ptrs[2] + 8 * (world + rank)
+            try:
+                for q in range(world):
+                    if q == rank:
+                        continue
+                    ptrs = []
+                    for h in every[q]:
+                        p = C.c_void_p()
+                        cabi.call("jo_ipc_open", C.create_string_buffer(h, len(h)), C.byref(p))
+                        ptrs.append(p.value)
+                        self._mapped.append(p.value)
+                    self.peer_k[q], self.peer_v[q] = ptrs[0], ptrs[1]
+                    self._ready_tab[q] = ptrs[2] + 8 * rank
+                    self._done_tab[q] = ptrs[2] + 8 * (world + rank)
+            except RuntimeError as e:
+                err = e
+            # every rank learns whether every rank mapped its peers, so all of them either use
+            # the gather or raise (and can fall back to the collective together)
+            ok = torch.tensor([0.0 if err else 1.0], device=dev)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if ok.item() < 1.0:
+                for p in self._mapped:
+                    cabi.status_of("jo_ipc_close", p)
+                self._mapped = []
+                dist.barrier(group=group)
+                self._flags.free()
+                raise RuntimeError(f"copy-engine K/V gather unavailable (rank {rank}: {err or 'a peer failed'})")
         self._local_ready = self._flags.ptr
         self._local_done = self._flags.ptr + 8 * world
         self.step = 0
