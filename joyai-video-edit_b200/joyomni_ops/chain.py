@@ -472,7 +472,8 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
                   w: BlockWeights, bufs: KVBuffers, group=None, rank: int = 0,
                   side_stream: Optional[torch.cuda.Stream] = None, trace: Optional[dict] = None,
                   events: Optional[dict] = None, mods: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                  store: bool = False, peers: Optional[PeerGather] = None):
+                  store: bool = False, peers: Optional[PeerGather] = None,
+                  text_stream: Optional[torch.cuda.Stream] = None):
     """One double-stream block for one chunk.
 
     img: bf16 [L_local, D] (this rank's video tokens), txt: bf16 [T_local, D] (this rank's
@@ -491,6 +492,11 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
     then replicates the chunk.
     ``peers`` (with ``group``): gather the chunk's K/V with the copy engines
     (``PeerGather``) instead of the NCCL all-gather.
+    ``text_stream``: run the text tokens' branches (LN + QKV + pack before attention, the
+    output projection and MLP after it) on this stream, beside the video tokens' branches on
+    the current stream: sharded over 4 or more ranks the text GEMMs fill 12-48 tiles only, so
+    alone they leave most SMs idle (with all 512 text rows on one GPU the overlap is slower);
+    the current stream waits for the text stream before attention and before returning.
     """
     H = w.heads
     L = img.shape[0]
@@ -502,10 +508,19 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
     k_pre = bufs.k_pre[bufs.spare][rank * bufs.local:(rank + 1) * bufs.local] if store else None
     if group is not None and peers is not None:
         peers.before_write(torch.cuda.current_stream())
+    cur = torch.cuda.current_stream()
+    if text_stream is not None:
+        text_stream.wait_stream(cur)
+        with torch.cuda.stream(text_stream):
+            _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows(rank)],
+                        bufs.v[bufs.txt_kv_rows(rank)], trace, "txt")
     _stream_qkv(img, w.img, mi, H, cos, sin, bufs.q[:L], bufs.k[bufs.img_kv_rows(rank)],
                 bufs.v[bufs.img_kv_rows(rank)], trace, "img", k_pre)
-    _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows(rank)],
-                bufs.v[bufs.txt_kv_rows(rank)], trace, "txt")
+    if text_stream is not None:
+        cur.wait_stream(text_stream)
+    else:
+        _stream_qkv(txt, w.txt, mt, H, None, None, bufs.q[L:], bufs.k[bufs.txt_kv_rows(rank)],
+                    bufs.v[bufs.txt_kv_rows(rank)], trace, "txt")
     gathered = None
     if group is not None:
         # complete the chunk's K/V (every rank's block) on a side stream; the attention
@@ -537,6 +552,14 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
         attn = attention(bufs.q, bufs.k, bufs.v)
     if trace is not None:
         trace.update({"q": bufs.q, "k": bufs.k, "v": bufs.v, "mi": mi, "mt": mt})
-    img_out = _stream_out(img, attn[:L], w.img, mi, trace, "img")
-    txt_out = _stream_out(txt, attn[L:], w.txt, mt, trace, "txt")
+    if text_stream is not None:
+        text_stream.wait_stream(cur)
+        with torch.cuda.stream(text_stream):
+            txt_out = _stream_out(txt, attn[L:], w.txt, mt, trace, "txt")
+        img_out = _stream_out(img, attn[:L], w.img, mi, trace, "img")
+        cur.wait_stream(text_stream)
+        txt_out.record_stream(cur)  # made on the text stream, used and freed on the caller's
+    else:
+        img_out = _stream_out(img, attn[:L], w.img, mi, trace, "img")
+        txt_out = _stream_out(txt, attn[L:], w.txt, mt, trace, "txt")
     return img_out, txt_out

@@ -96,10 +96,11 @@ def _block_worker(rank, world, port, q):
         bufs.v[:sp.CACHE].copy_(cv)
         peers = chain.PeerGather(bufs, rank, world, dist.group.WORLD)
         outs = []
-        for _ in range(2):
+        text = torch.cuda.Stream(dev)
+        for step in range(2):  # the second step with the text branches on their own stream
             a, b = chain.block_forward(img[b0:b1].to(dev), txt[t0:t1].to(dev), vec.to(dev), cos[b0:b1].to(dev),
                                        sin[b0:b1].to(dev), w, bufs, group=dist.group.WORLD, rank=rank,
-                                       peers=peers)
+                                       peers=peers, text_stream=text if step else None)
             torch.cuda.synchronize()
             outs.append((a.cpu(), b.cpu()))
         faults = cabi.device_fault_count()

@@ -76,3 +76,27 @@ def test_rank_shard_matches_single_gpu(single, dev, monkeypatch, world, rank):
         d = (got.float() - want.float()).abs().max().item()
         scale = want.float().abs().max().item()
         assert d <= 1e-2 * scale, f"rank {rank}/{world} differs from the single-GPU block by {d} (max |ref| {scale})"
+
+
+def test_text_stream_same_bits(single, dev, monkeypatch):
+    """The text tokens' branches on their own stream (``block_forward(..., text_stream=...)``,
+    what the bench does from 4 ranks on) give the same bits as on the current stream, at
+    the 8-rank shard shapes."""
+    from joyomni_ops import chain
+
+    s = single
+    world, rank = 8, 3
+    monkeypatch.setattr(chain, "gather_chunk_kv", lambda bufs, rank, group: None)
+    b0, b1 = chain.shard_range(IMG, world, rank)
+    t0, t1 = chain.shard_range(TXT, world, rank)
+    bufs = chain.KVBuffers(CACHE, IMG, TXT, HEADS, HD, world, dev)
+    bufs.k.copy_(s["k"][:bufs.k.shape[0]])
+    bufs.v.copy_(s["v"][:bufs.v.shape[0]])
+    outs = []
+    for ts in (None, torch.cuda.Stream()):
+        a, b = chain.block_forward(s["img"][b0:b1], s["txt"][t0:t1], s["vec"], s["cos"][b0:b1], s["sin"][b0:b1],
+                                   s["w"], bufs, group=object(), rank=rank, side_stream=torch.cuda.Stream(),
+                                   text_stream=ts)
+        torch.cuda.synchronize()
+        outs.append((a.clone(), b.clone()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
