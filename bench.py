@@ -474,8 +474,9 @@ class Chain(Workload):
             except RuntimeError as e:
                 note = f"{e}; the chunk K/V gathered by NCCL instead"
         # the text tokens' branches on their own stream beside the video tokens' (measured on one
-        # rank's shapes: 1058 -> 989 us per block at P = 8, 2-4 % at P = 4, slower at P = 1)
-        text = torch.cuda.Stream() if self.world >= 4 else None
+        # rank's shapes: 1058 -> 989 us per block at P = 8; at P = 4 2-4 % faster in three samples
+        # and 32 % slower in a fourth; slower at P = 2 and P = 1)
+        text = torch.cuda.Stream() if self.world >= 8 else None
         st = dict(chain=chain, w=w, img=img, txt=txt, vec=vec, cos=cos, sin=sin, bufs=bufs, side=side, peers=peers,
                   gather_note=note, text_stream=text)
         out = self.step(st)

@@ -494,8 +494,8 @@ def block_forward(img: torch.Tensor, txt: torch.Tensor, vec: torch.Tensor, cos: 
     (``PeerGather``) instead of the NCCL all-gather.
     ``text_stream``: run the text tokens' branches (LN + QKV + pack before attention, the
     output projection and MLP after it) on this stream, beside the video tokens' branches on
-    the current stream: sharded over 4 or more ranks the text GEMMs fill 12-48 tiles only, so
-    alone they leave most SMs idle (with all 512 text rows on one GPU the overlap is slower);
+    the current stream: sharded over 8 ranks the text GEMMs fill 12-48 tiles only, so alone
+    they leave most SMs idle (with 128 or more text rows per GPU the overlap was slower);
     the current stream waits for the text stream before attention and before returning.
     """
     H = w.heads
